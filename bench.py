@@ -1,0 +1,410 @@
+"""Benchmark of the iPC training step on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2] [--depth 6] [--act tanh]
+
+A *step* is one training step on one batch: T = 4 inference iterations
+(prediction + state update over all layers) followed by one weight update,
+after the forward-init sweep of the batch (the oracle schedule
+``for t in range(T): ipc_step(update_weights=(t == T-1))``).
+
+Default workload = ``configs[1]`` of the baseline: dims (10, 64 x depth, 784),
+depth 6, B = 128, fp16 storage / fp32 accumulation, alpha 1e-4, gamma 0.5,
+T = 4, f = tanh, 10 000 steps.  Inputs are seeded synthetic batches (MNIST is
+not available offline): a device pool of 1024 batches (205 MB, larger than
+the 126 MB L2), so every step reads a fresh batch from HBM.
+
+``value``: samples/s with the pool resident in HBM (persistent kernel,
+``TileLangIPC.train_pool``).  ``e2e``: the same through the public API with
+pinned host batches copied to the device and each step's energy copied back
+inside the timed region.  ``--gpus N`` runs N independent replicas (the
+hidden-64 network does not shard; weak scaling).  ``--impl reference`` times
+the reference's algorithm (the CPU oracle, a PyTorch restatement of
+``reference.py``) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+MEASURED_PEAKS = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+METRIC = "iPC train samples/s (T inf steps+1 W step)"
+
+
+# ----------------------------------------------------------------- helpers
+def peaks():
+    if MEASURED_PEAKS.exists():
+        d = json.loads(MEASURED_PEAKS.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {**FALLBACK_PEAKS, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.path is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "samples": len(rows), "reasons": reasons}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_info():
+    model = "unknown"
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return model, os.cpu_count() or 1
+
+
+# ------------------------------------------------------- algorithmic costs
+def step_costs(dims, B, T, elem):
+    """Algorithmic FLOP and bytes of one training step (forward init + T x (P + I) + W)."""
+    L = len(dims) - 1
+    mk = sum(dims[l] * dims[l + 1] for l in range(L))
+    km_inf = sum(dims[l] * dims[l - 1] for l in range(1, L))
+    init = sum(dims[l] * dims[l + 1] for l in range(1, L))
+    flop = 2 * B * (T * (mk + km_inf) + mk + init)
+    p = sum(elem * (dims[l] * dims[l + 1] + dims[l + 1] * B + 2 * dims[l] * B) for l in range(L))
+    i = sum(elem * (3 * dims[l] * B + dims[l - 1] * dims[l] + dims[l - 1] * B) for l in range(1, L))
+    w = sum(elem * (2 * dims[l] * dims[l + 1] + dims[l] * B + dims[l + 1] * B) for l in range(L))
+    return flop, T * (p + i) + w
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_baseline(dims, B, T, act, budget_s=12.0, max_steps=None):
+    """The reference algorithm (oracle restatement of reference.py, fp32) on all host cores."""
+    from lich_b200 import synthetic as S
+    from oracle import ipc_oracle as O
+    model, ncpu = cpu_info()
+    w = S.fan_in_normal(dims, seed=1)
+    pool = S.batch_pool(dims[-1], dims[0], B, count=4, seed=2)
+    # small GEMMs can run slower on many threads: keep the fastest of a few thread counts
+    best = (0.0, ncpu)
+    for th in sorted({ncpu, min(ncpu, 16), min(ncpu, 8), min(ncpu, 4)}, reverse=True):
+        torch.set_num_threads(th)
+        O.train_step(pool[0][0], pool[0][1], w, act=act, alpha=1e-4, gamma=0.5, T=T)
+        t0, k = time.perf_counter(), 0
+        while time.perf_counter() - t0 < min(1.0, budget_s / 8) and (max_steps is None or k < max_steps):
+            O.train_step(pool[k % 4][0], pool[k % 4][1], w, act=act, alpha=1e-4, gamma=0.5, T=T)
+            k += 1
+        rate = k / (time.perf_counter() - t0)
+        if rate > best[0]:
+            best = (rate, th)
+    cores = best[1]
+    torch.set_num_threads(cores)
+    w = S.fan_in_normal(dims, seed=1)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        x, w, e, _ = O.train_step(pool[n % 4][0], pool[n % 4][1], w, act=act, alpha=1e-4, gamma=0.5, T=T)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s or (max_steps is not None and n >= max_steps):
+            break
+    dt = time.perf_counter() - t0
+    return {"value": n * B / dt, "unit": "samples/s", "cores": cores, "kind": "port",
+            "sample": f"{n} training steps of B={B} (dims {list(dims)}, T={T}, {act}, fp32) in {dt:.1f} s "
+                      f"with torch.set_num_threads({cores}) on {model}"}
+
+
+# -------------------------------------------------------------- workloads
+def run_c2(args, world, rank, local):
+    from lich_b200 import _native as N
+    from lich_b200 import synthetic as S
+    from lich_b200.trainer import IPCConfig, TileLangIPC
+
+    dev = torch.device("cuda", local)
+    dtype = torch.float16
+    dims = S.paper_dims(args.depth)
+    B, T = 128, 4
+    cfg = IPCConfig(dims=dims, alpha=1e-4, gamma=0.5, activation=args.act, dtype=dtype)
+    model = TileLangIPC(cfg, device=dev, seed=rank)
+    for dst, src in zip(model.w, S.fan_in_normal(dims, seed=1 + rank)):
+        dst.copy_(src.to(dev, dtype))
+    assert model.net_kernel_eligible(B)
+
+    # device pool larger than L2: every step reads a fresh batch from HBM
+    P = 1024
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    pool_x = torch.rand((P, dims[-1], B), generator=g, device=dev).to(dtype)
+    labels = torch.randint(0, dims[0], (P, B), generator=g, device=dev)
+    pool_y = torch.zeros((P, dims[0], B), device=dev, dtype=dtype)
+    pool_y.scatter_(1, labels.unsqueeze(1), 1.0)
+
+    chunk = max(1, min(args.chunk, args.steps))
+    stream = torch.cuda.current_stream(dev)
+    # warm-up (untimed): W training steps
+    model.train_pool(pool_x, pool_y, steps=max(args.warmup, 1), T=T, first_batch=0)
+    torch.cuda.synchronize(dev)
+
+    launches0 = N.launch_count()
+    evs = []
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        done = 0
+        while done < args.steps:
+            n = min(chunk, args.steps - done)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            model.train_pool(pool_x, pool_y, steps=n, T=T, first_batch=(args.warmup + done) % P)
+            e1.record(stream)
+            evs.append((e0, e1, n))
+            done += n
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    launches = N.launch_count() - launches0
+    ms = start.elapsed_time(end)
+    ms_max = max_over_ranks(ms, world, dev)
+    per_launch = [(a.elapsed_time(b), n) for a, b, n in evs]
+
+    # roofline of the persistent kernel (the only kernel in the timed region)
+    flop_step, bytes_step = step_costs(dims, B, T, 2)
+    pk = peaks()
+    full = [(t, n) for t, n in per_launch if n == chunk] or per_launch
+    avg_ms = sum(t for t, _ in full) / len(full)
+    units = full[0][1]
+    achieved_gbs = bytes_step * units / (avg_ms * 1e-3) / 1e9
+    achieved_tfs = flop_step * units / (avg_ms * 1e-3) / 1e12
+    t_hbm = bytes_step / (pk["hbm_gbs"] * 1e9)
+    t_tc = flop_step / (pk["bf16_tflops"] * 1e12)
+    bound = "hbm" if t_hbm >= t_tc else "tensor"
+    roof = {"bound": bound, "achieved": round(achieved_gbs if bound == "hbm" else achieved_tfs, 2),
+            "peak": pk["hbm_gbs"] if bound == "hbm" else pk["bf16_tflops"],
+            "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
+            "frac": round((achieved_gbs / pk["hbm_gbs"]) if bound == "hbm" else (achieved_tfs / pk["bf16_tflops"]), 4),
+            "traffic": TRAFFIC_PER_STEP.get(("c2", args.depth)) and round(TRAFFIC_PER_STEP[("c2", args.depth)] * units),
+            "peak_source": pk["source"], "kernel": "net_kernel (ipc_net_train)",
+            "algorithmic_bytes_per_step": bytes_step, "algorithmic_flop_per_step": flop_step,
+            "steps_per_launch": units, "avg_launch_ms": round(avg_ms, 4),
+            "tensor_frac": round(achieved_tfs / pk["bf16_tflops"], 5)}
+
+    e2e = run_c2_e2e(args, model, dims, B, T, dtype, dev, rank, world)
+    value = world * args.steps * B / (ms_max * 1e-3)
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "samples/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 6),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"configs[1] paper efficiency: dims (10,64x{args.depth},784), B=128, T=4, "
+                               f"{args.act}, fp16 storage / fp32 accumulation, alpha 1e-4, gamma 0.5",
+                   "depth": args.depth, "batch": B, "T": T, "activation": args.act,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2: device pool of 1024 batches (205 MB) cycled, fresh batch per step",
+                   "steps_per_launch": chunk},
+        "roofline": roof, "e2e": e2e, "gpu_launches": int(launches), "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(dims, B, T, args.act)
+    return line
+
+
+# ncu dram__bytes_read.sum + dram__bytes_write.sum per training step of the persistent
+# kernel, from the captures summarised in profiles/ (filled in after each capture).
+TRAFFIC_PER_STEP: dict = {}
+
+
+def run_c2_e2e(args, model, dims, B, T, dtype, dev, rank, world):
+    """Public API, host batches: pinned host pool -> device ring (H2D in the timed region),
+    train_pool over the chunk, per-step energy copied back (D2H in the timed region)."""
+    from lich_b200 import synthetic as S
+    Ph = 64
+    x_h, y_h = S.stacked_pool(dims[-1], dims[0], B, count=Ph, nets=1, seed=77 + rank, dtype=dtype)
+    x_h = x_h[:, 0].contiguous().pin_memory()
+    y_h = y_h[:, 0].contiguous().pin_memory()
+    chunk = 64
+    steps = max(chunk, (min(args.steps, 4096) // chunk) * chunk)
+    ring_x = [torch.empty((chunk, dims[-1], B), device=dev, dtype=dtype) for _ in range(2)]
+    ring_y = [torch.empty((chunk, dims[0], B), device=dev, dtype=dtype) for _ in range(2)]
+    energy = [torch.empty((chunk,), device=dev, dtype=torch.float32) for _ in range(2)]
+    energy_h = torch.empty((steps,), dtype=torch.float32).pin_memory()
+    comp = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(dev)
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+
+    def h2d(slot, c):
+        with torch.cuda.stream(copy):
+            copy.wait_event(free[slot])
+            for j in range(chunk):
+                b = (c * chunk + j) % Ph
+                ring_x[slot][j].copy_(x_h[b], non_blocking=True)
+                ring_y[slot][j].copy_(y_h[b], non_blocking=True)
+            ready[slot].record(copy)
+
+    for s in range(2):
+        free[s].record(comp)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(comp)
+    nchunks = steps // chunk
+    h2d(0, 0)
+    for c in range(nchunks):
+        slot = c % 2
+        if c + 1 < nchunks:
+            h2d((c + 1) % 2, c + 1)
+        comp.wait_event(ready[slot])
+        model.train_pool(ring_x[slot], ring_y[slot], steps=chunk, T=T, energy=energy[slot])
+        energy_h[c * chunk:(c + 1) * chunk].copy_(energy[slot], non_blocking=True)
+        free[slot].record(comp)
+    end.record(comp)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(start.elapsed_time(end), world, dev)
+    assert torch.isfinite(energy_h).all()
+    h2d_b = (dims[-1] + dims[0]) * B * 2
+    return {"value": round(world * steps * B / (ms * 1e-3), 1), "unit": "samples/s", "h2d_bytes_per_step": h2d_b,
+            "d2h_bytes_per_step": 4, "steps": steps,
+            "path": "TileLangIPC.train_pool over pinned-host batches copied per chunk of 64 steps "
+                    "(copy stream, double-buffered), per-step energy read back"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference algorithm on the host CPU (rank 0 only)."""
+    if rank != 0:
+        return None
+    from lich_b200 import synthetic as S
+    dims = S.paper_dims(args.depth)
+    B, T = 128, 4
+    budget = max(5.0, min(120.0, 0.005 * args.steps + 2.0))
+    cb = cpu_baseline(dims, B, T, args.act, budget_s=budget)
+    return {"metric": METRIC, "value": round(cb["value"], 1), "unit": "samples/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(B / cb["value"] * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"configs[1] paper efficiency: dims (10,64x{args.depth},784), B=128, T=4, "
+                                   f"{args.act}", "depth": args.depth, "batch": B, "T": T},
+            "cpu_baseline": cb,
+            "e2e": {"value": round(cb["value"], 1), "unit": "samples/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["c2"], default="c2")
+    ap.add_argument("--depth", type=int, default=6)
+    ap.add_argument("--act", default="tanh")
+    ap.add_argument("--chunk", type=int, default=500, help="training steps per persistent-kernel launch")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    world, rank, local = dist_setup(args)
+    line = run_c2(args, world, rank, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

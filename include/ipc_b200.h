@@ -1,0 +1,190 @@
+/*
+ * ipc_b200.h -- C ABI of the B200 (sm_100a) incremental-predictive-coding step.
+ *
+ * These entry points replace the three fused TileLang operators of
+ * laghzen/Lich (package ipc_tilelang) and the trainer's per-step launch loop.
+ * Every function takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*; NULL = legacy default stream), allocates
+ * nothing, and returns IPC_OK (0) or a negative IPC_ERR_* code; the message
+ * of the last failure on the calling thread is ipc_last_error().
+ *
+ * Layout (reference README.md:43-50): activations are feature-major,
+ * row-major [features, batch]; W[l] is row-major [d_l, d_{l+1}]; grouped
+ * operands are `groups` such matrices stacked contiguously.  Storage dtype
+ * is one of IPC_DT_*; accumulation is always fp32.  Kernels mutate their
+ * in/out operands in place, like the reference kernels.
+ */
+#ifndef IPC_B200_H
+#define IPC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IPC_ABI_VERSION 1
+
+/* return codes */
+#define IPC_OK 0
+#define IPC_ERR_ARG (-1)         /* bad shape / flag / pointer (reference raises ValueError) */
+#define IPC_ERR_UNSUPPORTED (-2) /* valid request this build cannot serve */
+#define IPC_ERR_CUDA (-3)        /* a CUDA runtime call failed; see ipc_last_error() */
+#define IPC_ERR_TIMEOUT (-4)     /* a bounded device-side wait gave up */
+#define IPC_ERR_DEVICE (-5)      /* no sm_100 device current */
+
+/* activations (reference src/ipc_tilelang/activations.py:6-29; identity from
+ * weight_update_specialization.py:86) */
+#define IPC_ACT_RELU 0
+#define IPC_ACT_TANH 1
+#define IPC_ACT_SIGMOID 2
+#define IPC_ACT_SILU 3
+#define IPC_ACT_GELU 4 /* tanh approximation */
+#define IPC_ACT_IDENTITY 5
+
+/* storage dtypes */
+#define IPC_DT_F32 0
+#define IPC_DT_F16 1
+#define IPC_DT_BF16 2
+
+/* algorithm selector (`algo` argument); IPC_ALGO_AUTO picks by shape */
+#define IPC_ALGO_AUTO 0
+#define IPC_ALGO_SIMT 1    /* tiled CUDA-core / mma.sync kernel, any shape */
+#define IPC_ALGO_TCGEN05 2 /* tcgen05 + TMEM + TMA tensor-core kernel (16-bit storage) */
+#define IPC_ALGO_OUTER 3   /* weight update only: outer-product kernel for small B */
+
+/* Library identity: IPC_ABI_VERSION. */
+int ipc_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* ipc_last_error(void);
+
+/* Number of kernels this library has launched since load (all entry points). */
+unsigned long long ipc_launch_count(void);
+
+/*
+ * Prediction + error:  E[g] = cast(X_lo[g]) - cast(W[g] @ f(X_up[g]))
+ *   x_up [groups, K, B], w [groups, M, K], x_lo [groups, M, B], e [groups, M, B].
+ * Replaces build_prediction_error (src/ipc_tilelang/tilelang_kernels.py:114-177)
+ * and build_prediction_error_batched (src/ipc_tilelang/layer_batching.py:89-150).
+ */
+int ipc_pred_err(const void* x_up, const void* w, const void* x_lo, void* e,
+                 int M, int K, int B, int groups, int act, int dtype, int algo, void* stream);
+
+/*
+ * Prediction + error from a saved activation: same as ipc_pred_err but the
+ * first operand is A = f(X_up) already, so no activation is applied.
+ * Used by the save-A schedule; no reference counterpart (the reference always
+ * recomputes f in this operator, tilelang_kernels.py:159-167).
+ */
+int ipc_pred_err_saved(const void* a_up, const void* w, const void* x_lo, void* e,
+                       int M, int K, int B, int groups, int dtype, int algo, void* stream);
+
+/*
+ * Inference update:  X[g] += gamma * (-E[g] + f'(X[g]) * (W_low[g]^T @ E_low[g]))
+ *   x [groups, M, B] (in/out), e [groups, M, B], w_low [groups, K, M],
+ *   e_low [groups, K, B], a_out [groups, M, B] or NULL.
+ * When a_out is non-NULL it receives f(x_new) (save-activation variant).
+ * Replaces build_inference_update (tilelang_kernels.py:180-265) and
+ * build_inference_update_batched (layer_batching.py:153-248).
+ */
+int ipc_infer_update(void* x, const void* e, const void* w_low, const void* e_low, void* a_out,
+                     int M, int K, int B, int groups, float gamma, int act, int dtype, int algo,
+                     void* stream);
+
+/*
+ * Weight update:  W[g] = cast(W[g] + alpha * E[g] @ A[g]^T)
+ *   w [groups, M, K] (in/out), e [groups, M, B], x_up [groups, K, B].
+ * recompute != 0: A = f(x_up);  recompute == 0: x_up already holds A.
+ * algo IPC_ALGO_OUTER selects the small-batch outer-product kernel (any B,
+ * intended for B <= 16).  The sign is +alpha for every algorithm (the
+ * reference's eager small-B path subtracts, weight_update_specialization.py:102;
+ * its GEMM kernel and its oracle add, tilelang_kernels.py:320, reference.py:57).
+ * Replaces build_weight_update (tilelang_kernels.py:268-349),
+ * build_weight_update_batched (layer_batching.py:251-346) and
+ * SmallBWeightUpdater (weight_update_specialization.py:63-128).
+ */
+int ipc_weight_update(void* w, const void* e, const void* x_up, int M, int K, int B, int groups,
+                      float alpha, int recompute, int act, int dtype, int algo, void* stream);
+
+/*
+ * Weight delta in fp32 without touching W (data-parallel path):
+ *   dw[g] (+)= alpha * E[g] @ A[g]^T ; accumulate != 0 adds into dw.
+ * Followed by a sum-allreduce of dw across ranks and ipc_weight_apply.
+ * No reference counterpart (the reference is single-GPU).
+ */
+int ipc_weight_delta(float* dw, const void* e, const void* x_up, int M, int K, int B, int groups,
+                     float alpha, int recompute, int accumulate, int act, int dtype, int algo,
+                     void* stream);
+
+/* W = cast(float(W) + dw) over n elements (the epilogue of ipc_weight_update, split off). */
+int ipc_weight_apply(void* w, const float* dw, long long n, int dtype, void* stream);
+
+/*
+ * Forward prediction:  OUT[g] = cast(W[g] @ f(X_up[g]))
+ *   x_up [groups, K, B], w [groups, M, K], out [groups, M, B].
+ * The forward-init sweep of TileLangIPC.initialize_batch (trainer.py:512-515)
+ * and the layers of TileLangIPC.predict (trainer.py:828-833), which the
+ * reference runs as eager torch matmuls.
+ */
+int ipc_forward(const void* x_up, const void* w, void* out, int M, int K, int B, int groups, int act, int dtype,
+                int algo, void* stream);
+
+/* A = cast(f(X)) over n elements (materialise a saved activation). */
+int ipc_activate(void* a, const void* x, long long n, int act, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Persistent multi-layer network kernel (small widths).
+ *
+ * One launch runs `steps` training steps of `nets` independent networks.
+ * Network n's buffers are the n-th slab of each stacked array below.
+ * A training step is: (optionally) load a batch from the pool into x[L] and
+ * x[0]; (optionally) the forward-init sweep x[l] = W[l] f(x[l+1]),
+ * l = L-1..1 (trainer.py:509-516); T inference iterations, each all
+ * prediction errors then all state updates (trainer.py:609-638); then, if
+ * update_weights, W[l] += alpha e[l] f(x[l+1])^T for every l with the errors
+ * of the last iteration and the updated states (reference.py:52-57).
+ * With pool == NULL, forward_init == 0, T == 1 and update_weights == 1 a call
+ * is exactly TileLangIPC.step_initialized (trainer.py:601-679).
+ * Limits: 1 <= L <= IPC_NET_MAX_LAYERS; hidden widths d_1..d_{L-1} <= 64;
+ * d_0 <= 64; d_L any; B a multiple of 8 and <= 256; 16-bit storage.
+ * --------------------------------------------------------------------------- */
+#define IPC_NET_MAX_LAYERS 8
+
+typedef struct ipc_net {
+  int L;                            /* number of weight matrices */
+  int dims[IPC_NET_MAX_LAYERS + 1]; /* d_0 (classes) .. d_L (input) */
+  int B;                            /* batch columns per network */
+  int nets;                         /* independent networks */
+  void* w[IPC_NET_MAX_LAYERS];      /* W[l]: [nets, d_l, d_{l+1}] */
+  void* x[IPC_NET_MAX_LAYERS + 1];  /* x[l]: [nets, d_l, B] */
+  void* e[IPC_NET_MAX_LAYERS + 1];  /* e[l]: [nets, d_l, B] (e[L] unused, may be NULL) */
+} ipc_net_t;
+
+typedef struct ipc_net_run {
+  const void* pool_x; /* [pool_batches, nets, d_L, B] or NULL (use x[L] as is) */
+  const void* pool_y; /* [pool_batches, nets, d_0, B] or NULL (use x[0] as is) */
+  int pool_batches;
+  int first_batch;    /* step s uses batch (first_batch + s) % pool_batches */
+  int steps;          /* training steps in this launch */
+  int T;              /* inference iterations per training step */
+  int forward_init;   /* run the forward-init sweep at the start of each step */
+  int update_weights; /* weight update after the T-th iteration */
+  int recompute;      /* 1: f recomputed from stored x (reference recompute mode) */
+  float alpha, gamma;
+  int act, dtype;
+  int cluster;        /* CTAs per network (0 = auto) */
+  float* energy;      /* [steps, nets] or NULL: sum_l<L mean(e[l]^2) of the last iteration of
+                         each step (reference.py:58); zeroed by the call */
+} ipc_net_run_t;
+
+/* Replaces the TileLangIPC.step_initialized launch loop (trainer.py:601-679)
+ * and the steady-state graph of IPCGraphRunner (cuda_graph.py:22-31). */
+int ipc_net_train(const ipc_net_t* net, const ipc_net_run_t* run, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IPC_B200_H */

@@ -1,0 +1,159 @@
+"""ctypes binding of the C ABI in ``include/ipc_b200.h`` (``lich_b200/_lib/libipc_b200.so``).
+
+The library is the product: there is no CPU or eager-torch fallback.  If it is
+missing, importing the operators raises immediately with the build command.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, Structure, c_char_p, c_float, c_int, c_longlong, c_ulonglong, c_void_p
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libipc_b200.so"
+
+IPC_OK = 0
+IPC_ERR_ARG = -1
+IPC_ERR_UNSUPPORTED = -2
+IPC_ERR_CUDA = -3
+IPC_ERR_TIMEOUT = -4
+IPC_ERR_DEVICE = -5
+
+ACT_CODES = {"relu": 0, "tanh": 1, "sigmoid": 2, "silu": 3, "gelu": 4, "identity": 5, "linear": 5}
+DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+DTYPE_NAMES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16,
+               "fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16,
+               "half": torch.float16}
+ALGO_CODES = {"auto": 0, "simt": 1, "generic": 1, "tcgen05": 2, "outer": 3}
+
+NET_MAX_LAYERS = 8
+
+EXPORTED = (
+    "ipc_abi_version", "ipc_last_error", "ipc_launch_count", "ipc_pred_err", "ipc_pred_err_saved",
+    "ipc_forward", "ipc_infer_update", "ipc_weight_update", "ipc_weight_delta", "ipc_weight_apply",
+    "ipc_activate", "ipc_net_train",
+)
+
+
+class IpcNet(Structure):
+    _fields_ = [
+        ("L", c_int),
+        ("dims", c_int * (NET_MAX_LAYERS + 1)),
+        ("B", c_int),
+        ("nets", c_int),
+        ("w", c_void_p * NET_MAX_LAYERS),
+        ("x", c_void_p * (NET_MAX_LAYERS + 1)),
+        ("e", c_void_p * (NET_MAX_LAYERS + 1)),
+    ]
+
+
+class IpcNetRun(Structure):
+    _fields_ = [
+        ("pool_x", c_void_p),
+        ("pool_y", c_void_p),
+        ("pool_batches", c_int),
+        ("first_batch", c_int),
+        ("steps", c_int),
+        ("T", c_int),
+        ("forward_init", c_int),
+        ("update_weights", c_int),
+        ("recompute", c_int),
+        ("alpha", c_float),
+        ("gamma", c_float),
+        ("act", c_int),
+        ("dtype", c_int),
+        ("cluster", c_int),
+        ("energy", c_void_p),
+    ]
+
+
+class IpcError(RuntimeError):
+    """A C-ABI call returned a negative code."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"ipc error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the native library; raise if it was not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = Path(os.environ.get("LICH_B200_LIB", LIB_PATH))
+    if not path.exists():
+        raise RuntimeError(f"native library {path} is missing: build it with `python -m lich_b200.build`")
+    lib = ctypes.CDLL(str(path))
+    vp, i, f, ll = c_void_p, c_int, c_float, c_longlong
+    sig = {
+        "ipc_abi_version": (i, []),
+        "ipc_last_error": (c_char_p, []),
+        "ipc_launch_count": (c_ulonglong, []),
+        "ipc_pred_err": (i, [vp, vp, vp, vp, i, i, i, i, i, i, i, vp]),
+        "ipc_pred_err_saved": (i, [vp, vp, vp, vp, i, i, i, i, i, i, vp]),
+        "ipc_forward": (i, [vp, vp, vp, i, i, i, i, i, i, i, vp]),
+        "ipc_infer_update": (i, [vp, vp, vp, vp, vp, i, i, i, i, f, i, i, i, vp]),
+        "ipc_weight_update": (i, [vp, vp, vp, i, i, i, i, f, i, i, i, i, vp]),
+        "ipc_weight_delta": (i, [vp, vp, vp, i, i, i, i, f, i, i, i, i, i, vp]),
+        "ipc_weight_apply": (i, [vp, vp, ll, i, vp]),
+        "ipc_activate": (i, [vp, vp, ll, i, i, vp]),
+        "ipc_net_train": (i, [POINTER(IpcNet), POINTER(IpcNetRun), vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc != IPC_OK:
+        msg = load().ipc_last_error().decode(errors="replace")
+        if rc == IPC_ERR_ARG:
+            raise ValueError(f"ipc error {rc}: {msg}")
+        raise IpcError(rc, msg)
+
+
+def stream_handle(device: torch.device | None = None) -> int:
+    """The current torch CUDA stream as a raw cudaStream_t value."""
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def act_code(name: str) -> int:
+    try:
+        return ACT_CODES[str(name).lower()]
+    except KeyError as exc:
+        raise ValueError(f"Unsupported activation {name!r}") from exc
+
+
+def dtype_code(dtype) -> int:
+    if isinstance(dtype, str):
+        if dtype not in DTYPE_NAMES:
+            raise ValueError(f"Unsupported dtype {dtype!r}")
+        dtype = DTYPE_NAMES[dtype]
+    try:
+        return DTYPE_CODES[dtype]
+    except KeyError as exc:
+        raise ValueError(f"Unsupported dtype {dtype!r}") from exc
+
+
+def torch_dtype(dtype) -> torch.dtype:
+    if isinstance(dtype, str):
+        if dtype not in DTYPE_NAMES:
+            raise ValueError(f"Unsupported dtype {dtype!r}")
+        return DTYPE_NAMES[dtype]
+    return dtype
+
+
+def launch_count() -> int:
+    return int(load().ipc_launch_count())

@@ -1,0 +1,199 @@
+// C ABI entry points (include/ipc_b200.h): argument checks, algorithm choice,
+// error reporting.  No allocation happens here; all buffers are caller-owned.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "ipc_common.cuh"
+#include "ipc_elementwise.cuh"
+#include "ipc_generic.cuh"
+#include "ipc_tc.cuh"
+
+namespace ipc {
+
+namespace {
+thread_local char g_last_error[512] = "";
+std::atomic<unsigned long long> g_launches{0};
+int g_arch_ok[64] = {0};  // 0 unknown, 1 sm_100, -1 other
+}  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(err));
+  return IPC_OK;
+}
+
+void count_launch(unsigned long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+int require_sm100() {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return set_error(IPC_ERR_DEVICE, "no CUDA device: %s", cudaGetErrorString(err));
+  if (dev >= 0 && dev < 64 && g_arch_ok[dev] == 1) return IPC_OK;
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0) {
+    if (dev >= 0 && dev < 64) g_arch_ok[dev] = -1;
+    return set_error(IPC_ERR_DEVICE, "this library is built for sm_100a (B200); device %d is sm_%d%d", dev, major,
+                     minor);
+  }
+  if (dev >= 0 && dev < 64) g_arch_ok[dev] = 1;
+  return IPC_OK;
+}
+
+}  // namespace ipc
+
+using namespace ipc;
+
+#define IPC_REQUIRE(cond, ...) \
+  do {                         \
+    if (!(cond)) return set_error(IPC_ERR_ARG, __VA_ARGS__); \
+  } while (0)
+
+static int common_checks(int M, int K, int B, int groups, int act, int dtype, int algo) {
+  IPC_REQUIRE(M >= 0 && K >= 0 && B >= 0, "negative size (M=%d K=%d B=%d)", M, K, B);
+  IPC_REQUIRE(groups >= 1, "groups must be >= 1 (got %d)", groups);
+  IPC_REQUIRE(act >= IPC_ACT_RELU && act <= IPC_ACT_IDENTITY, "unknown activation code %d", act);
+  IPC_REQUIRE(dtype >= IPC_DT_F32 && dtype <= IPC_DT_BF16, "unknown dtype code %d", dtype);
+  IPC_REQUIRE(algo >= IPC_ALGO_AUTO && algo <= IPC_ALGO_OUTER, "unknown algo code %d", algo);
+  return require_sm100();
+}
+
+extern "C" {
+
+int ipc_abi_version(void) { return IPC_ABI_VERSION; }
+
+const char* ipc_last_error(void) { return g_last_error; }
+
+unsigned long long ipc_launch_count(void) { return g_launches.load(); }
+
+static int pred_err_impl(const void* x_up, const void* w, const void* x_lo, void* e, int M, int K, int B,
+                         int groups, int act, int dtype, int algo, void* stream, bool bact) {
+  int rc = common_checks(M, K, B, groups, act, dtype, algo);
+  if (rc) return rc;
+  IPC_REQUIRE(algo != IPC_ALGO_OUTER, "IPC_ALGO_OUTER applies to the weight update only");
+  if (M == 0 || B == 0) return IPC_OK;
+  IPC_REQUIRE(x_lo && e && (K == 0 || (x_up && w)), "null operand pointer");
+  GemmArgs p{};
+  p.A = w; p.lda = K; p.gsA = (long long)M * K;
+  p.Bm = x_up; p.ldb = B; p.gsB = (long long)K * B;
+  p.Mg = M; p.Ng = B; p.Kg = K; p.groups = groups;
+  p.out = e; p.gsOut = (long long)M * B;
+  p.aux = x_lo; p.gsAux = (long long)M * B;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (tc_eligible(MODE_P, M, K, B, dtype, algo)) return launch_tc(p, MODE_P, bact, act, dtype, s);
+  if (algo == IPC_ALGO_TCGEN05) return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: shape/dtype not eligible (M=%d K=%d B=%d dtype=%d)", M, K, B, dtype);
+  return launch_generic(p, MODE_P, bact, act, dtype, s);
+}
+
+int ipc_pred_err(const void* x_up, const void* w, const void* x_lo, void* e, int M, int K, int B, int groups,
+                 int act, int dtype, int algo, void* stream) {
+  return pred_err_impl(x_up, w, x_lo, e, M, K, B, groups, act, dtype, algo, stream, true);
+}
+
+int ipc_pred_err_saved(const void* a_up, const void* w, const void* x_lo, void* e, int M, int K, int B, int groups,
+                       int dtype, int algo, void* stream) {
+  return pred_err_impl(a_up, w, x_lo, e, M, K, B, groups, IPC_ACT_IDENTITY, dtype, algo, stream, false);
+}
+
+int ipc_forward(const void* x_up, const void* w, void* out, int M, int K, int B, int groups, int act, int dtype,
+                int algo, void* stream) {
+  int rc = common_checks(M, K, B, groups, act, dtype, algo);
+  if (rc) return rc;
+  IPC_REQUIRE(algo != IPC_ALGO_OUTER, "IPC_ALGO_OUTER applies to the weight update only");
+  if (M == 0 || B == 0) return IPC_OK;
+  IPC_REQUIRE(out && (K == 0 || (x_up && w)), "null operand pointer");
+  GemmArgs p{};
+  p.A = w; p.lda = K; p.gsA = (long long)M * K;
+  p.Bm = x_up; p.ldb = B; p.gsB = (long long)K * B;
+  p.Mg = M; p.Ng = B; p.Kg = K; p.groups = groups;
+  p.out = out; p.gsOut = (long long)M * B;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (tc_eligible(MODE_F, M, K, B, dtype, algo)) return launch_tc(p, MODE_F, true, act, dtype, s);
+  if (algo == IPC_ALGO_TCGEN05) return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: shape/dtype not eligible (M=%d K=%d B=%d dtype=%d)", M, K, B, dtype);
+  return launch_generic(p, MODE_F, true, act, dtype, s);
+}
+
+int ipc_infer_update(void* x, const void* e, const void* w_low, const void* e_low, void* a_out, int M, int K, int B,
+                     int groups, float gamma, int act, int dtype, int algo, void* stream) {
+  int rc = common_checks(M, K, B, groups, act, dtype, algo);
+  if (rc) return rc;
+  IPC_REQUIRE(algo != IPC_ALGO_OUTER, "IPC_ALGO_OUTER applies to the weight update only");
+  if (M == 0 || B == 0) return IPC_OK;
+  IPC_REQUIRE(x && e && (K == 0 || (w_low && e_low)), "null operand pointer");
+  GemmArgs p{};
+  p.A = w_low; p.lda = M; p.gsA = (long long)K * M;
+  p.Bm = e_low; p.ldb = B; p.gsB = (long long)K * B;
+  p.Mg = M; p.Ng = B; p.Kg = K; p.groups = groups;
+  p.out = x; p.gsOut = (long long)M * B;
+  p.aux = e; p.gsAux = (long long)M * B;
+  p.aux2 = a_out; p.gsAux2 = (long long)M * B;
+  p.scale = gamma;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (tc_eligible(MODE_I, M, K, B, dtype, algo)) return launch_tc(p, MODE_I, false, act, dtype, s);
+  if (algo == IPC_ALGO_TCGEN05) return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: shape/dtype not eligible (M=%d K=%d B=%d dtype=%d)", M, K, B, dtype);
+  return launch_generic(p, MODE_I, false, act, dtype, s);
+}
+
+static int weight_impl(void* out, const void* e, const void* x_up, int M, int K, int B, int groups, float alpha,
+                       int recompute, int accumulate, int act, int dtype, int algo, void* stream, bool delta) {
+  int rc = common_checks(M, K, B, groups, act, dtype, algo);
+  if (rc) return rc;
+  if (M == 0 || K == 0) return IPC_OK;
+  IPC_REQUIRE(out && (B == 0 || (e && x_up)), "null operand pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool bact = recompute != 0;
+  if (algo == IPC_ALGO_OUTER || (algo == IPC_ALGO_AUTO && B <= 16))
+    return launch_outer(out, e, x_up, M, K, B, groups, alpha, bact, delta, accumulate, act, dtype, s);
+  GemmArgs p{};
+  p.A = e; p.lda = B; p.gsA = (long long)M * B;
+  p.Bm = x_up; p.ldb = B; p.gsB = (long long)K * B;
+  p.Mg = M; p.Ng = K; p.Kg = B; p.groups = groups;
+  p.out = out; p.gsOut = (long long)M * K;
+  p.scale = alpha;
+  p.accumulate = accumulate;
+  const int mode = delta ? MODE_WD : MODE_W;
+  if (tc_eligible(mode, M, K, B, dtype, algo)) return launch_tc(p, mode, bact, act, dtype, s);
+  if (algo == IPC_ALGO_TCGEN05) return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: shape/dtype not eligible (M=%d K=%d B=%d dtype=%d)", M, K, B, dtype);
+  return launch_generic(p, mode, bact, act, dtype, s);
+}
+
+int ipc_weight_update(void* w, const void* e, const void* x_up, int M, int K, int B, int groups, float alpha,
+                      int recompute, int act, int dtype, int algo, void* stream) {
+  return weight_impl(w, e, x_up, M, K, B, groups, alpha, recompute, 0, act, dtype, algo, stream, false);
+}
+
+int ipc_weight_delta(float* dw, const void* e, const void* x_up, int M, int K, int B, int groups, float alpha,
+                     int recompute, int accumulate, int act, int dtype, int algo, void* stream) {
+  return weight_impl(dw, e, x_up, M, K, B, groups, alpha, recompute, accumulate, act, dtype, algo, stream, true);
+}
+
+int ipc_weight_apply(void* w, const float* dw, long long n, int dtype, void* stream) {
+  int rc = common_checks(1, 1, 1, 1, IPC_ACT_IDENTITY, dtype, IPC_ALGO_AUTO);
+  if (rc) return rc;
+  IPC_REQUIRE(n >= 0, "negative element count");
+  if (n == 0) return IPC_OK;
+  IPC_REQUIRE(w && dw, "null operand pointer");
+  return launch_apply(w, dw, n, dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ipc_activate(void* a, const void* x, long long n, int act, int dtype, void* stream) {
+  int rc = common_checks(1, 1, 1, 1, act, dtype, IPC_ALGO_AUTO);
+  if (rc) return rc;
+  IPC_REQUIRE(n >= 0, "negative element count");
+  if (n == 0) return IPC_OK;
+  IPC_REQUIRE(a && x, "null operand pointer");
+  return launch_activate(a, x, n, act, dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

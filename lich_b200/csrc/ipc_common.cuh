@@ -1,0 +1,132 @@
+// Shared device helpers: activations, storage types, error plumbing.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/ipc_b200.h"
+
+namespace ipc {
+
+// ---------------------------------------------------------------------------
+// Activations.  f and f' follow src/ipc_tilelang/activations.py:9-29 and the
+// in-kernel forms of src/ipc_tilelang/tilelang_kernels.py:61-96; they are
+// always evaluated in fp32 (the reference kernels evaluate f' on the fp32 up-
+// cast of the stored x, tilelang_kernels.py:227-229).  tanh/exp are CUDA's
+// own tanhf/expf.
+// ---------------------------------------------------------------------------
+constexpr float kGeluC = 0.044715f;
+constexpr float kGeluK = 0.7978845608028654f;
+
+template <int ACT>
+__device__ __forceinline__ float act_f(float x) {
+  if constexpr (ACT == IPC_ACT_RELU) {
+    return x > 0.f ? x : 0.f;
+  } else if constexpr (ACT == IPC_ACT_TANH) {
+    return tanhf(x);
+  } else if constexpr (ACT == IPC_ACT_SIGMOID) {
+    return 1.f / (1.f + expf(-x));
+  } else if constexpr (ACT == IPC_ACT_SILU) {
+    return x / (1.f + expf(-x));
+  } else if constexpr (ACT == IPC_ACT_GELU) {
+    float u = kGeluK * (x + kGeluC * x * x * x);
+    return 0.5f * x * (1.f + tanhf(u));
+  } else {
+    return x;
+  }
+}
+
+template <int ACT>
+__device__ __forceinline__ float act_df(float x) {
+  if constexpr (ACT == IPC_ACT_RELU) {
+    return x > 0.f ? 1.f : 0.f;
+  } else if constexpr (ACT == IPC_ACT_TANH) {
+    float y = tanhf(x);
+    return 1.f - y * y;
+  } else if constexpr (ACT == IPC_ACT_SIGMOID) {
+    float y = 1.f / (1.f + expf(-x));
+    return y * (1.f - y);
+  } else if constexpr (ACT == IPC_ACT_SILU) {
+    float s = 1.f / (1.f + expf(-x));
+    return s * (1.f + x * (1.f - s));
+  } else if constexpr (ACT == IPC_ACT_GELU) {
+    float u = kGeluK * (x + kGeluC * x * x * x);
+    float t = tanhf(u);
+    float du = kGeluK * (1.f + 3.f * kGeluC * x * x);
+    return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * du;
+  } else {
+    return 1.f;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Storage types.
+// ---------------------------------------------------------------------------
+template <typename T>
+struct St;
+template <>
+struct St<float> {
+  static __device__ __forceinline__ float ld(float v) { return v; }
+  static __device__ __forceinline__ float st(float v) { return v; }
+  static constexpr int code = IPC_DT_F32;
+};
+template <>
+struct St<__half> {
+  static __device__ __forceinline__ float ld(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half st(float v) { return __float2half_rn(v); }
+  static constexpr int code = IPC_DT_F16;
+};
+template <>
+struct St<__nv_bfloat16> {
+  static __device__ __forceinline__ float ld(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 st(float v) { return __float2bfloat16_rn(v); }
+  static constexpr int code = IPC_DT_BF16;
+};
+
+// Round an fp32 value through the storage type (the reference's T.cast).
+template <typename T>
+__device__ __forceinline__ float rnd(float v) {
+  return St<T>::ld(St<T>::st(v));
+}
+
+// ---------------------------------------------------------------------------
+// Host-side error plumbing (defined in ipc_abi.cu).
+// ---------------------------------------------------------------------------
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+void count_launch(unsigned long long n = 1);
+int require_sm100();
+
+// Dispatch helpers: turn runtime act / dtype codes into template arguments.
+#define IPC_DISPATCH_ACT(act, ACTC, ...)                                   \
+  switch (act) {                                                            \
+    case IPC_ACT_RELU: { constexpr int ACTC = IPC_ACT_RELU; __VA_ARGS__; break; }       \
+    case IPC_ACT_TANH: { constexpr int ACTC = IPC_ACT_TANH; __VA_ARGS__; break; }       \
+    case IPC_ACT_SIGMOID: { constexpr int ACTC = IPC_ACT_SIGMOID; __VA_ARGS__; break; } \
+    case IPC_ACT_SILU: { constexpr int ACTC = IPC_ACT_SILU; __VA_ARGS__; break; }       \
+    case IPC_ACT_GELU: { constexpr int ACTC = IPC_ACT_GELU; __VA_ARGS__; break; }       \
+    case IPC_ACT_IDENTITY: { constexpr int ACTC = IPC_ACT_IDENTITY; __VA_ARGS__; break; } \
+    default: return set_error(IPC_ERR_ARG, "unknown activation code %d", act);        \
+  }
+
+#define IPC_DISPATCH_DT(dtype, TT, ...)                                    \
+  switch (dtype) {                                                          \
+    case IPC_DT_F32: { using TT = float; __VA_ARGS__; break; }              \
+    case IPC_DT_F16: { using TT = __half; __VA_ARGS__; break; }             \
+    case IPC_DT_BF16: { using TT = __nv_bfloat16; __VA_ARGS__; break; }     \
+    default: return set_error(IPC_ERR_ARG, "unknown dtype code %d", dtype); \
+  }
+
+#define IPC_DISPATCH_DT16(dtype, TT, ...)                                   \
+  switch (dtype) {                                                           \
+    case IPC_DT_F16: { using TT = __half; __VA_ARGS__; break; }              \
+    case IPC_DT_BF16: { using TT = __nv_bfloat16; __VA_ARGS__; break; }      \
+    default: return set_error(IPC_ERR_UNSUPPORTED, "dtype code %d: this kernel needs 16-bit storage", dtype); \
+  }
+
+inline size_t dt_size(int dtype) { return dtype == IPC_DT_F32 ? 4 : 2; }
+
+}  // namespace ipc

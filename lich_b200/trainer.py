@@ -1,0 +1,600 @@
+"""iPC trainer -- the drop-in for ``ipc_tilelang.trainer`` (``IPCConfig``, ``TileLangIPC``, ``prepare_batch``).
+
+Same constructor, attributes and methods as the reference
+(``src/ipc_tilelang/trainer.py:28-846``); the step runs on sm_100a kernels:
+
+* **net path** (16-bit storage, every width except the input <= 64, B a
+  multiple of 8 up to 256, recompute mode): one launch of the persistent
+  multi-layer kernel (``ipc_net_train``) per call -- ``step_initialized`` is
+  one launch instead of the reference's 3L-1, and a whole training step
+  (forward-init sweep, T inference iterations, weight update) is also one
+  launch (``train_step`` / ``train_pool``);
+* **operator path** (anything else: fp32, wide layers, save-activation
+  mode): the fused P / I / W operators in the reference's phase order
+  (``trainer.py:609-674``), with grid.z layer batching of square internal
+  layers (``layer_batching.find_internal_square_groups``).
+
+Additions (no reference counterpart): ``step_initialized(update_weights=)``
+for the "T inference iterations + 1 weight update" schedule,
+``train_step`` / ``train_pool`` / ``run_inference``, and
+``state_dict`` / ``load_state_dict``.
+
+The sm_86 tuning caches the reference consults (``hierarchical_policy.json``,
+``gridz_policy.json``) do not describe this hardware; the policy fields of
+``IPCConfig`` are accepted and recorded but the sm_100a kernels pick their own
+tiles, and grid.z grouping uses ``grid_z_max_layers`` directly.
+"""
+from __future__ import annotations
+
+from dataclasses import asdict, dataclass, field
+from typing import Sequence
+
+import torch
+
+from . import _native as N
+from .activations import get_activation
+from .layer_batching import (
+    LayerBatchGroup,
+    build_forward_batched,
+    build_inference_update_batched,
+    build_prediction_error_batched,
+    build_weight_update_batched,
+    find_internal_square_groups,
+)
+from .tilelang_kernels import (
+    KernelConfig,
+    build_forward,
+    build_inference_update,
+    build_prediction_error,
+    build_weight_update,
+)
+from .tuning import TuningTable
+from .weight_update_specialization import SmallBWeightPolicy, SmallBWeightUpdater
+
+TARGET_CAPABILITY = (10, 0)
+
+
+def one_hot(labels: torch.Tensor, num_classes: int, *, dtype: torch.dtype) -> torch.Tensor:
+    """``[C, B]`` one-hot target on the labels' device (reference ``reference.py:12-13``)."""
+    y = torch.zeros((num_classes, labels.numel()), dtype=dtype, device=labels.device)
+    y.scatter_(0, labels.reshape(1, -1).long(), 1.0)
+    return y
+
+
+@dataclass(frozen=True)
+class IPCConfig:
+    dims: tuple[int, ...]
+    alpha: float = 1e-4
+    gamma: float = 0.5
+    activation: str = "relu"
+    dtype: torch.dtype = torch.float16
+    kernel: KernelConfig = KernelConfig()
+    recompute_activation: bool = True
+    tuning_table: TuningTable | None = None
+    use_grid_z: bool = True
+    grid_z_max_layers: int = 2
+    grid_z_auto: bool = True
+    grid_z_policy_path: str = "results/gridz_policy.json"
+    hierarchical_policy_auto: bool = True
+    hierarchical_policy_path: str = "results/hierarchical_policy.json"
+    steady_state_graph_auto: bool = True
+    steady_state_graph_default: bool = False
+    weight_update_mode: str = "gemm"
+    weight_update_policy_path: str = "results/weight_update_policy.json"
+    weight_update_outer_max_batch: int = 16
+    # sm_100a additions
+    use_net_kernel: bool = True
+    net_cluster: int = 0
+
+
+class TileLangIPC:
+    """iPC MLP trainer on one B200; see the module docstring."""
+
+    def __init__(self, cfg: IPCConfig, *, device: torch.device, seed: int = 0):
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise ValueError("TileLangIPC requires a CUDA device")
+        cap = torch.cuda.get_device_capability(device)
+        if cap != TARGET_CAPABILITY:
+            raise ValueError(f"lich_b200 is built for sm_100a (B200); got capability {cap}")
+        if len(cfg.dims) < 2:
+            raise ValueError("dims needs at least two entries")
+        self.cfg = cfg
+        self.device = device
+        self.act = get_activation(cfg.activation)
+        N.dtype_code(cfg.dtype)
+        self._runtime_recompute_activation = bool(cfg.recompute_activation)
+        self._grid_z_cap = max(0, int(cfg.grid_z_max_layers))
+        self._layer_groups: tuple[LayerBatchGroup, ...] = (
+            find_internal_square_groups(tuple(cfg.dims), max_group_count=self._grid_z_cap)
+            if cfg.use_grid_z and self._grid_z_cap >= 2 else ()
+        )
+        self._edge_to_group = {l: gi for gi, g in enumerate(self._layer_groups) for l in g.edge_indices}
+
+        # Weight init: kaiming_uniform_(a=sqrt(5)) in layer order from one device generator,
+        # grouped layers stored in one [G, D, D] tensor (reference trainer.py:88-108).
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        self.w: list[torch.Tensor] = [None] * (len(cfg.dims) - 1)  # type: ignore[list-item]
+        self._w_grouped = [torch.empty((gr.count, gr.width, gr.width), device=device, dtype=cfg.dtype)
+                           for gr in self._layer_groups]
+        for l, (n_l, n_u) in enumerate(zip(cfg.dims[:-1], cfg.dims[1:])):
+            gi = self._edge_to_group.get(l)
+            w = (torch.empty((n_l, n_u), device=device, dtype=cfg.dtype) if gi is None
+                 else self._w_grouped[gi][l - self._layer_groups[gi].start])
+            torch.nn.init.kaiming_uniform_(w, a=5 ** 0.5, generator=g)
+            self.w[l] = w
+
+        self.x: list[torch.Tensor] | None = None
+        self.e: list[torch.Tensor] | None = None
+        self.a: list[torch.Tensor | None] | None = None
+        self._x_grouped: list[torch.Tensor] = []
+        self._e_grouped: list[torch.Tensor] = []
+        self._a_grouped: list[torch.Tensor] | None = None
+        self._runtime_plan_key: tuple | None = None
+        self._pred_singleton_kernels: list[object | None] = []
+        self._inf_singleton_kernels: list[object | None] = []
+        self._weight_singleton_kernels: list[object | None] = []
+        self._fwd_singleton_kernels: list[object | None] = []
+        self._pred_singleton_ops: tuple = ()
+        self._inf_singleton_ops: tuple = ()
+        self._weight_singleton_ops: tuple = ()
+        self._pred_group_kernels: tuple = ()
+        self._inf_group_kernels: tuple = ()
+        self._weight_group_kernels: tuple = ()
+        self._weight_singleton_outer_ops: tuple = ()
+        self._weight_group_outer_ops: tuple = ()
+        self._steady_state_runner = None
+        self._steady_state_graph_key: tuple | None = None
+        self._steady_state_graph_steps: int | None = None
+        self._net_desc = None
+        self._net_keep = None
+        self.steps_done = 0
+        self._weight_update_policy: SmallBWeightPolicy | None = None
+        self._small_b_updater = SmallBWeightUpdater(alpha=float(cfg.alpha))
+        if str(cfg.weight_update_mode).lower() == "auto":
+            try:
+                self._weight_update_policy = SmallBWeightPolicy(cfg.weight_update_policy_path)
+            except Exception:
+                self._weight_update_policy = None
+
+    # ------------------------------------------------------------------ info
+    @property
+    def L(self) -> int:
+        return len(self.w)
+
+    @property
+    def recompute_activation(self) -> bool:
+        return bool(self._runtime_recompute_activation)
+
+    @property
+    def dtype_name(self) -> str:
+        return str(self.cfg.dtype).split(".")[-1]
+
+    def net_kernel_eligible(self, batch: int | None = None) -> bool:
+        """Whether ``step_initialized`` / ``train_pool`` run as one persistent-kernel launch."""
+        d = self.cfg.dims
+        ok = (self.cfg.use_net_kernel and self.cfg.dtype in (torch.float16, torch.bfloat16)
+              and self.recompute_activation and 1 <= self.L <= N.NET_MAX_LAYERS
+              and all(int(v) <= 64 for v in d[:-1]))
+        if batch is not None:
+            B = int(batch)
+            if self.cfg.net_cluster > 0:
+                C = int(self.cfg.net_cluster)
+                ok = ok and B % C == 0 and B // C in (8, 16, 32) and C <= 16
+            else:
+                ok = ok and any(B % n == 0 and B // n <= 8 for n in (16, 8, 32))
+        return bool(ok)
+
+    def recommended_use_cuda_graph(self, batch: int | None = None, *, default: bool = False) -> bool:
+        """Graph replay pays off whenever the step is launch-bound; the net path is one launch already."""
+        return bool(default)
+
+    def runtime_plan_ready(self) -> bool:
+        return self._runtime_plan_key is not None
+
+    def _grouped_edge_indices(self) -> frozenset[int]:
+        return frozenset(self._edge_to_group)
+
+    # ---------------------------------------------------------------- buffers
+    def _invalidate_steady_state_graph(self) -> None:
+        self._steady_state_runner = None
+        self._steady_state_graph_key = None
+        self._steady_state_graph_steps = None
+
+    def _ensure_buffers(self, B: int) -> None:
+        if self.x is not None and self.x[0].shape[1] == B:
+            return
+        self._invalidate_steady_state_graph()
+        self._net_desc = None
+        dims = self.cfg.dims
+        dt, dev = self.cfg.dtype, self.device
+        self.x = [None] * len(dims)  # type: ignore[list-item]
+        self.e = [None] * len(dims)  # type: ignore[list-item]
+        self._x_grouped, self._e_grouped = [], []
+        self.a = None if self.recompute_activation else [None] * len(dims)
+        self._a_grouped = None if self.recompute_activation else []
+        grouped_states = set()
+        for gi, gr in enumerate(self._layer_groups):
+            xbuf = torch.zeros((gr.state_count, gr.width, B), device=dev, dtype=dt)
+            ebuf = torch.zeros_like(xbuf)
+            self._x_grouped.append(xbuf)
+            self._e_grouped.append(ebuf)
+            if self._a_grouped is not None:
+                self._a_grouped.append(torch.zeros_like(xbuf))
+            for z, layer in enumerate(gr.state_indices):
+                grouped_states.add(layer)
+                self.x[layer] = xbuf[z]
+                self.e[layer] = ebuf[z]
+                if self.a is not None:
+                    self.a[layer] = self._a_grouped[gi][z]
+        for layer, d in enumerate(dims):
+            if layer in grouped_states:
+                continue
+            self.x[layer] = torch.zeros((d, B), device=dev, dtype=dt)
+            self.e[layer] = torch.zeros_like(self.x[layer])
+            if self.a is not None:
+                self.a[layer] = torch.zeros_like(self.x[layer])
+        self._runtime_plan_key = None
+
+    def _prepare_runtime_plan(self, batch: int) -> None:
+        """Build the kernel-call plan once per (dims, batch, activation, dtype, mode)."""
+        key = (tuple(int(d) for d in self.cfg.dims), int(batch), self.cfg.activation, self.dtype_name,
+               self.recompute_activation, self._grid_z_cap)
+        if key == self._runtime_plan_key:
+            return
+        B = int(batch)
+        d = self.cfg.dims
+        act, dt, kc = self.cfg.activation, self.dtype_name, self.cfg.kernel
+        grouped = self._grouped_edge_indices()
+        grouped_inf = {l for gr in self._layer_groups for l in range(gr.start + 1, gr.end + 2)}
+        pred = [None] * self.L
+        inf = [None] * self.L
+        wgt = [None] * self.L
+        fwd = [None] * self.L
+        outer_single = []
+        for l in range(self.L):
+            fwd[l] = build_forward(d[l], d[l + 1], B, act, dt, kc)
+            if l not in grouped:
+                pred[l] = build_prediction_error(d[l], d[l + 1], B, act, dt, kc)
+                M, K = d[l], d[l + 1]
+                if self._outer_weight_enabled(M, K, B):
+                    op = self._small_b_updater.make_singleton(M=M, K=K, B=B, activation=act, dtype=self.cfg.dtype)
+                    if op is not None:
+                        outer_single.append((l, op))
+                        continue
+                wgt[l] = build_weight_update(d[l], d[l + 1], B, act, dt, kc, self.cfg.alpha,
+                                             self.recompute_activation)
+        for l in range(1, self.L):
+            if l not in grouped_inf:
+                inf[l] = build_inference_update(d[l], d[l - 1], B, act, dt, kc, self.cfg.gamma,
+                                                not self.recompute_activation)
+        pg, ig, wg, og = [], [], [], []
+        for gr in self._layer_groups:
+            pg.append(build_prediction_error_batched(gr.width, gr.width, B, gr.count, act, dt, kc))
+            ig.append(build_inference_update_batched(gr.width, gr.width, B, gr.count, act, dt, kc, self.cfg.gamma,
+                                                     not self.recompute_activation))
+            outer = None
+            if self._outer_weight_enabled(gr.width, gr.width, B, gr.count):
+                outer = self._small_b_updater.make_grouped(count=gr.count, M=gr.width, K=gr.width, B=B,
+                                                           activation=act, dtype=self.cfg.dtype)
+            og.append(outer)
+            wg.append(None if outer is not None else build_weight_update_batched(
+                gr.width, gr.width, B, gr.count, act, dt, kc, self.cfg.alpha, self.recompute_activation))
+        self._pred_singleton_kernels, self._inf_singleton_kernels = pred, inf
+        self._weight_singleton_kernels, self._fwd_singleton_kernels = wgt, fwd
+        self._weight_singleton_outer_ops = tuple(outer_single)
+        self._pred_singleton_ops = tuple((l, k) for l, k in enumerate(pred) if k is not None)
+        self._inf_singleton_ops = tuple((l, k) for l, k in enumerate(inf) if k is not None)
+        self._weight_singleton_ops = tuple((l, k) for l, k in enumerate(wgt) if k is not None)
+        self._pred_group_kernels, self._inf_group_kernels = tuple(pg), tuple(ig)
+        self._weight_group_kernels, self._weight_group_outer_ops = tuple(wg), tuple(og)
+        self._runtime_plan_key = key
+
+    def _outer_weight_enabled(self, M: int, K: int, B: int, count: int = 1) -> bool:
+        mode = str(self.cfg.weight_update_mode).lower()
+        if mode == "outer":
+            return True
+        if mode != "auto" or int(B) > int(self.cfg.weight_update_outer_max_batch):
+            return False
+        if self._weight_update_policy is None:
+            return True  # measured crossover on B200: the outer kernel wins for B <= 16
+        return self._weight_update_policy.backend(M=M, K=K, B=B, activation=self.cfg.activation,
+                                                  dtype=self.cfg.dtype, count=count) == "outer"
+
+    # ------------------------------------------------------------ net kernel
+    def _net(self):
+        if self._net_desc is None:
+            desc = N.IpcNet()
+            desc.L = self.L
+            for l, dv in enumerate(self.cfg.dims):
+                desc.dims[l] = int(dv)
+            desc.B = int(self.x[0].shape[1])
+            desc.nets = 1
+            for l in range(self.L):
+                desc.w[l] = self.w[l].data_ptr()
+                desc.e[l] = self.e[l].data_ptr()
+            for l in range(self.L + 1):
+                desc.x[l] = self.x[l].data_ptr()
+            self._net_desc = desc
+        return self._net_desc
+
+    def _net_run(self, *, steps: int, T: int, forward_init: bool, update_weights: bool,
+                 pool_x: torch.Tensor | None = None, pool_y: torch.Tensor | None = None, first_batch: int = 0,
+                 energy: torch.Tensor | None = None):
+        run = N.IpcNetRun()
+        if energy is not None:
+            if energy.dtype != torch.float32 or energy.numel() < steps or not energy.is_contiguous() \
+                    or energy.device != self.device:
+                raise ValueError("energy must be a contiguous float32 tensor with >= steps elements on the model device")
+            run.energy = energy.data_ptr()
+        run.pool_x = None if pool_x is None else pool_x.data_ptr()
+        run.pool_y = None if pool_y is None else pool_y.data_ptr()
+        run.pool_batches = 0 if pool_x is None else int(pool_x.shape[0])
+        run.first_batch = int(first_batch)
+        run.steps, run.T = int(steps), int(T)
+        run.forward_init, run.update_weights = int(forward_init), int(update_weights)
+        run.recompute = 1
+        run.alpha, run.gamma = float(self.cfg.alpha), float(self.cfg.gamma)
+        run.act, run.dtype = self.act.code, N.dtype_code(self.cfg.dtype)
+        run.cluster = int(self.cfg.net_cluster)
+        N.check(N.load().ipc_net_train(self._net(), run, N.stream_handle(self.device)))
+
+    # ----------------------------------------------------------------- steps
+    def initialize_batch(self, x_input: torch.Tensor, y_target: torch.Tensor) -> None:
+        """Reset endpoints and initialise hidden states by a forward prediction (reference :453-516)."""
+        if x_input.ndim != 2 or y_target.ndim != 2:
+            raise ValueError("Inputs must be [features, batch]")
+        B = int(x_input.shape[1])
+        if x_input.shape[0] != self.cfg.dims[-1] or y_target.shape[0] != self.cfg.dims[0]:
+            raise ValueError("Batch dimensions do not match network dims")
+        if y_target.shape[1] != B:
+            raise ValueError("input and target batch sizes differ")
+        self._ensure_buffers(B)
+        self._prepare_runtime_plan(B)
+        self.x[-1].copy_(x_input)
+        if self.a is not None:
+            self.a[-1].copy_(self.act.forward(self.x[-1]))
+        for l in reversed(range(1, self.L)):
+            self._fwd_singleton_kernels[l](self.x[l + 1], self.w[l], self.x[l])
+        self.x[0].copy_(y_target)
+
+    @torch.no_grad()
+    def step_initialized(self, *, collect_metrics: bool = False, update_weights: bool = True) -> dict[str, float]:
+        """P for all layers, I for the hidden layers, then (by default) W for all layers
+        (reference ``trainer.py:601-679``); one launch on the net path."""
+        if self.x is None or self.e is None:
+            raise RuntimeError("Call initialize_batch before step_initialized")
+        B = int(self.x[-1].shape[1])
+        if self._runtime_plan_key is None:
+            self._prepare_runtime_plan(B)
+        if self.net_kernel_eligible(B):
+            self._net_run(steps=1, T=1, forward_init=False, update_weights=update_weights)
+        else:
+            self._phase_p()
+            self._phase_i()
+            if update_weights:
+                self._phase_w()
+        if update_weights:
+            self.steps_done += 1
+        if collect_metrics:
+            return self.metrics()
+        return {}
+
+    def _phase_p(self):
+        for gi, gr in enumerate(self._layer_groups):
+            xs, es = self._x_grouped[gi], self._e_grouped[gi]
+            self._pred_group_kernels[gi](xs[1:], self._w_grouped[gi], xs[:-1], es[:-1])
+        for l, k in self._pred_singleton_ops:
+            k(self.x[l + 1], self.w[l], self.x[l], self.e[l])
+
+    def _phase_i(self):
+        for gi, gr in enumerate(self._layer_groups):
+            xs, es, ws = self._x_grouped[gi], self._e_grouped[gi], self._w_grouped[gi]
+            if self.a is None:
+                self._inf_group_kernels[gi](xs[1:], es[1:], ws, es[:-1])
+            else:
+                self._inf_group_kernels[gi](xs[1:], es[1:], ws, es[:-1], self._a_grouped[gi][1:])
+        for l, k in self._inf_singleton_ops:
+            if self.a is None:
+                k(self.x[l], self.e[l], self.w[l - 1], self.e[l - 1])
+            else:
+                k(self.x[l], self.e[l], self.w[l - 1], self.e[l - 1], self.a[l])
+
+    def _phase_w(self):
+        for gi, gr in enumerate(self._layer_groups):
+            es, ws = self._e_grouped[gi], self._w_grouped[gi]
+            src = self._x_grouped[gi][1:] if self.a is None else self._a_grouped[gi][1:]
+            op = self._weight_group_outer_ops[gi] if self._weight_group_outer_ops else None
+            (op if op is not None else self._weight_group_kernels[gi])(ws, es[:-1], src)
+        for l, op in self._weight_singleton_outer_ops:
+            op(self.w[l], self.e[l], self.x[l + 1] if self.a is None else self.a[l + 1])
+        for l, k in self._weight_singleton_ops:
+            k(self.w[l], self.e[l], self.x[l + 1] if self.a is None else self.a[l + 1])
+
+    def metrics(self) -> dict[str, float]:
+        """``max |e[l]|`` over ``l < L`` (reference ``trainer.py:676-678``); synchronises."""
+        return {"max_abs_error": float(max(v.float().abs().max().item() for v in self.e[:-1]))}
+
+    @torch.no_grad()
+    def step(self, x_input: torch.Tensor, y_target: torch.Tensor) -> dict[str, float]:
+        self.initialize_batch(x_input, y_target)
+        return self.step_initialized(collect_metrics=True)
+
+    @torch.no_grad()
+    def run_inference(self, T: int) -> None:
+        """T inference iterations (P + I) without a weight update."""
+        for _ in range(int(T)):
+            self.step_initialized(update_weights=False)
+
+    @torch.no_grad()
+    def train_step(self, x_input: torch.Tensor, y_target: torch.Tensor, *, T: int = 4,
+                   collect_metrics: bool = False) -> dict[str, float]:
+        """One training step: forward-init sweep, T inference iterations, one weight update
+        with the last iteration's errors and states (the oracle schedule
+        ``for t in range(T): ipc_step(update_weights=(t == T-1))``)."""
+        B = int(x_input.shape[1])
+        if T < 1:
+            raise ValueError("T must be >= 1")
+        if self.net_kernel_eligible(B):
+            if x_input.shape[0] != self.cfg.dims[-1] or y_target.shape[0] != self.cfg.dims[0]:
+                raise ValueError("Batch dimensions do not match network dims")
+            self._ensure_buffers(B)
+            self._prepare_runtime_plan(B)
+            self.x[-1].copy_(x_input)
+            self.x[0].copy_(y_target)
+            self._net_run(steps=1, T=T, forward_init=True, update_weights=True)
+            self.steps_done += 1
+        else:
+            self.initialize_batch(x_input, y_target)
+            for t in range(T):
+                self.step_initialized(update_weights=(t == T - 1))
+        return self.metrics() if collect_metrics else {}
+
+    @torch.no_grad()
+    def train_pool(self, pool_x: torch.Tensor, pool_y: torch.Tensor, *, steps: int, T: int = 4,
+                   first_batch: int = 0, energy: torch.Tensor | None = None) -> None:
+        """``steps`` training steps over a device-resident batch pool.
+
+        ``pool_x [P, d_L, B]`` and ``pool_y [P, d_0, B]`` (contiguous, model dtype, on the
+        model's device); step ``s`` trains on batch ``(first_batch + s) % P``.  On the net
+        path this is a single kernel launch.  ``energy`` (float32, >= steps elements, net
+        path only) receives each step's ``sum_l mean(e[l]^2)`` of its last iteration."""
+        if pool_x.ndim != 3 or pool_y.ndim != 3:
+            raise ValueError("pool_x / pool_y must be [P, features, batch]")
+        P, dL, B = pool_x.shape
+        if dL != self.cfg.dims[-1] or pool_y.shape[1] != self.cfg.dims[0] or pool_y.shape[0] != P \
+                or pool_y.shape[2] != B:
+            raise ValueError("pool shapes do not match network dims")
+        for t in (pool_x, pool_y):
+            if t.device != self.device or t.dtype != self.cfg.dtype or not t.is_contiguous():
+                raise ValueError("pool tensors must be contiguous, on the model device, in the model dtype")
+        if steps <= 0:
+            return
+        if self.net_kernel_eligible(B):
+            self._ensure_buffers(int(B))
+            self._prepare_runtime_plan(int(B))
+            self._net_run(steps=steps, T=T, forward_init=True, update_weights=True, pool_x=pool_x, pool_y=pool_y,
+                          first_batch=first_batch, energy=energy)
+            self.steps_done += int(steps)
+        else:
+            if energy is not None:
+                raise ValueError("per-step energy output needs the persistent-kernel path")
+            for s in range(int(steps)):
+                b = (first_batch + s) % P
+                self.train_step(pool_x[b], pool_y[b], T=T)
+
+    # ---------------------------------------------------------- steady state
+    def steady_state_graph_ready(self, steps: int) -> bool:
+        return (self._steady_state_runner is not None and self._steady_state_graph_steps == int(steps)
+                and self._steady_state_graph_key == self._runtime_plan_key)
+
+    def prepare_steady_state(self, x_input: torch.Tensor, y_target: torch.Tensor, *, steps: int = 1,
+                             use_graph: bool | None = None) -> bool:
+        """Reference ``trainer.py:693-724``: initialise the batch; capture ``steps`` steps if graphs are on."""
+        steps = max(1, int(steps))
+        self.initialize_batch(x_input, y_target)
+        if use_graph is None:
+            use_graph = bool(self.cfg.steady_state_graph_default)
+        if not use_graph:
+            return False
+        if not self.steady_state_graph_ready(steps):
+            self._steady_state_runner = self.capture_graph(steps)
+            self._steady_state_graph_steps = steps
+            self._steady_state_graph_key = self._runtime_plan_key
+        return True
+
+    @torch.no_grad()
+    def run_prepared_steady_state(self, *, steps: int | None = None, repeats: int = 1,
+                                  use_graph: bool | None = None, collect_metrics: bool = False) -> dict[str, float]:
+        if self.x is None or self.e is None or self._runtime_plan_key is None:
+            raise RuntimeError("Call prepare_steady_state/initialize_batch first")
+        steps = max(1, int(self._steady_state_graph_steps if steps is None else steps))
+        repeats = max(1, int(repeats))
+        if use_graph is None:
+            use_graph = self.steady_state_graph_ready(steps)
+        if use_graph:
+            if not self.steady_state_graph_ready(steps):
+                raise RuntimeError("Requested graph replay without a matching captured graph")
+            for _ in range(repeats):
+                self._steady_state_runner.replay()
+        else:
+            for _ in range(repeats):
+                for _ in range(steps):
+                    self.step_initialized(collect_metrics=False)
+        torch.cuda.synchronize(self.device)
+        return self.metrics() if collect_metrics else {}
+
+    def reset_steady_state(self) -> None:
+        self._invalidate_steady_state_graph()
+
+    @property
+    def steady_state_uses_graph(self) -> bool:
+        return self._steady_state_runner is not None
+
+    def run_steady_state_batch(self, x_input, y_target, *, steps: int = 1, repeats: int = 1,
+                               use_graph: bool | None = None, collect_metrics: bool = False) -> dict[str, float]:
+        self.prepare_steady_state(x_input, y_target, steps=steps, use_graph=use_graph)
+        return self.run_prepared_steady_state(steps=steps, repeats=repeats, use_graph=use_graph,
+                                              collect_metrics=collect_metrics)
+
+    def precompile(self) -> None:
+        """Run one step with the state saved and restored, so every kernel's one-time
+        attribute setup happens outside any graph capture (reference ``trainer.py:783-818``)."""
+        if self.x is None or self.e is None:
+            raise RuntimeError("Call initialize_batch before precompile")
+        self._prepare_runtime_plan(int(self.x[-1].shape[1]))
+        saved = [t.clone() for t in self.w + self.x + self.e] + \
+                ([v.clone() for v in self.a if v is not None] if self.a is not None else [])
+        done = self.steps_done
+        self.step_initialized(collect_metrics=False)
+        torch.cuda.synchronize(self.device)
+        live = list(self.w + self.x + self.e) + ([v for v in self.a if v is not None] if self.a is not None else [])
+        for dst, src in zip(live, saved):
+            dst.copy_(src)
+        self.steps_done = done
+        torch.cuda.synchronize(self.device)
+
+    def capture_graph(self, steps: int):
+        if self.x is None or self.e is None:
+            raise RuntimeError("Call initialize_batch before capture_graph")
+        from .cuda_graph import IPCGraphRunner
+        runner = IPCGraphRunner(self, steps)
+        runner.capture()
+        return runner
+
+    @torch.no_grad()
+    def predict(self, x_input: torch.Tensor) -> torch.Tensor:
+        """``h = W[l] @ f(h)`` for ``l = L-1..0`` (reference ``trainer.py:828-833``)."""
+        h = x_input.contiguous()
+        B = int(h.shape[1])
+        for l in reversed(range(self.L)):
+            out = torch.empty((self.cfg.dims[l], B), device=self.device, dtype=self.cfg.dtype)
+            build_forward(self.cfg.dims[l], self.cfg.dims[l + 1], B, self.cfg.activation, self.dtype_name,
+                          self.cfg.kernel)(h, self.w[l], out)
+            h = out
+        return h
+
+    # ---------------------------------------------------------- checkpoints
+    def state_dict(self) -> dict:
+        return {"dims": tuple(self.cfg.dims), "w": [w.detach().clone() for w in self.w],
+                "steps_done": int(self.steps_done),
+                "config": {k: (str(v) if k in ("dtype", "kernel", "tuning_table") else v)
+                           for k, v in asdict(self.cfg).items() if k != "tuning_table"}}
+
+    def load_state_dict(self, state: dict) -> None:
+        if tuple(state["dims"]) != tuple(self.cfg.dims):
+            raise ValueError(f"checkpoint dims {state['dims']} != model dims {self.cfg.dims}")
+        for dst, src in zip(self.w, state["w"]):
+            if tuple(src.shape) != tuple(dst.shape):
+                raise ValueError("checkpoint weight shape mismatch")
+            dst.copy_(src.to(device=self.device, dtype=self.cfg.dtype))
+        self.steps_done = int(state.get("steps_done", 0))
+
+
+def prepare_batch(images: torch.Tensor, labels: torch.Tensor, *, device: torch.device, dtype: torch.dtype,
+                  num_classes: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """NCHW images -> ``[784, B]`` input, labels -> ``[C, B]`` one-hot (reference ``trainer.py:836-846``)."""
+    x = images.flatten(1).T.contiguous().to(device=device, dtype=dtype, non_blocking=True)
+    y = one_hot(labels.to(device, non_blocking=True), num_classes, dtype=dtype)
+    return x, y

@@ -1,0 +1,26 @@
+"""Reader for the committed golden vectors in ``tests/golden/*.npz``."""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import torch
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def cases():
+    return sorted(p.stem for p in GOLDEN.glob("*.npz"))
+
+
+def load(name: str):
+    z = np.load(GOLDEN / f"{name}.npz")
+    meta = json.loads(str(z["meta"]))
+    L = len(meta["dims"]) - 1
+    t = lambda k: torch.from_numpy(z[k].copy())  # noqa: E731
+    w_in = [t(f"w_in_{i}") for i in range(L)]
+    w_out = [t(f"w_out_{i}") for i in range(L)]
+    x_out = [t(f"x_out_{i}") for i in range(L + 1)]
+    batches = [(t(f"xb_{j}"), t(f"yb_{j}")) for j in range(meta["batches"])]
+    return meta, w_in, batches, w_out, x_out
