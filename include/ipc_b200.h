@@ -147,8 +147,9 @@ int ipc_activate(void* a, const void* x, long long n, int act, int dtype, void* 
  * of the last iteration and the updated states (reference.py:52-57).
  * With pool == NULL, forward_init == 0, T == 1 and update_weights == 1 a call
  * is exactly TileLangIPC.step_initialized (trainer.py:601-679).
- * Limits: 1 <= L <= IPC_NET_MAX_LAYERS; hidden widths d_1..d_{L-1} <= 64;
- * d_0 <= 64; d_L any; B a multiple of 8 and <= 256; 16-bit storage.
+ * Limits: 1 <= L <= IPC_NET_MAX_LAYERS; d_0 .. d_{L-1} <= 64; d_L a multiple
+ * of 8; B a multiple of 8 and <= 256; 16-bit storage; the per-CTA layout must
+ * fit in shared memory (ipc_net_plan answers).
  * --------------------------------------------------------------------------- */
 #define IPC_NET_MAX_LAYERS 8
 
@@ -178,6 +179,12 @@ typedef struct ipc_net_run {
   float* energy;      /* [steps, nets] or NULL: sum_l<L mean(e[l]^2) of the last iteration of
                          each step (reference.py:58); zeroed by the call */
 } ipc_net_run_t;
+
+/* Whether ipc_net_train can run this network: IPC_OK and the cluster size
+ * (CTAs per network) and dynamic shared memory per CTA it would use, or an
+ * IPC_ERR_* code.  cluster = 0 lets the library choose.  Launches nothing.
+ * No reference counterpart (a planning query of the persistent kernel). */
+int ipc_net_plan(const ipc_net_t* net, int cluster, int* cluster_out, int* smem_bytes_out);
 
 /* Replaces the TileLangIPC.step_initialized launch loop (trainer.py:601-679)
  * and the steady-state graph of IPCGraphRunner (cuda_graph.py:22-31). */

@@ -33,7 +33,7 @@ NET_MAX_LAYERS = 8
 EXPORTED = (
     "ipc_abi_version", "ipc_last_error", "ipc_launch_count", "ipc_pred_err", "ipc_pred_err_saved",
     "ipc_forward", "ipc_infer_update", "ipc_weight_update", "ipc_weight_delta", "ipc_weight_apply",
-    "ipc_activate", "ipc_net_train",
+    "ipc_activate", "ipc_net_train", "ipc_net_plan",
 )
 
 
@@ -103,6 +103,7 @@ def load() -> ctypes.CDLL:
         "ipc_weight_apply": (i, [vp, vp, ll, i, vp]),
         "ipc_activate": (i, [vp, vp, ll, i, i, vp]),
         "ipc_net_train": (i, [POINTER(IpcNet), POINTER(IpcNetRun), vp]),
+        "ipc_net_plan": (i, [POINTER(IpcNet), i, POINTER(c_int), POINTER(c_int)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -153,6 +154,20 @@ def torch_dtype(dtype) -> torch.dtype:
             raise ValueError(f"Unsupported dtype {dtype!r}")
         return DTYPE_NAMES[dtype]
     return dtype
+
+
+def net_plan(dims, B: int, nets: int = 1, cluster: int = 0) -> tuple[int, int] | None:
+    """(cluster, shared-memory bytes) the persistent kernel would use, or None if it cannot run."""
+    desc = IpcNet()
+    desc.L = len(dims) - 1
+    if not 1 <= desc.L <= NET_MAX_LAYERS:
+        return None
+    for l, d in enumerate(dims):
+        desc.dims[l] = int(d)
+    desc.B, desc.nets = int(B), int(nets)
+    c, sm = c_int(0), c_int(0)
+    rc = load().ipc_net_plan(ctypes.byref(desc), int(cluster), ctypes.byref(c), ctypes.byref(sm))
+    return (c.value, sm.value) if rc == IPC_OK else None
 
 
 def launch_count() -> int:

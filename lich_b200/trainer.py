@@ -177,13 +177,8 @@ class TileLangIPC:
         ok = (self.cfg.use_net_kernel and self.cfg.dtype in (torch.float16, torch.bfloat16)
               and self.recompute_activation and 1 <= self.L <= N.NET_MAX_LAYERS
               and all(int(v) <= 64 for v in d[:-1]))
-        if batch is not None:
-            B = int(batch)
-            if self.cfg.net_cluster > 0:
-                C = int(self.cfg.net_cluster)
-                ok = ok and B % C == 0 and B // C in (8, 16, 32) and C <= 16
-            else:
-                ok = ok and any(B % n == 0 and B // n <= 8 for n in (16, 8, 32))
+        if batch is not None and ok:
+            ok = N.net_plan(d, int(batch), 1, int(self.cfg.net_cluster)) is not None
         return bool(ok)
 
     def recommended_use_cuda_graph(self, batch: int | None = None, *, default: bool = False) -> bool:
