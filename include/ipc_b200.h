@@ -178,7 +178,15 @@ typedef struct ipc_net_run {
   int cluster;        /* CTAs per network (0 = auto) */
   float* energy;      /* [steps, nets] or NULL: sum_l<L mean(e[l]^2) of the last iteration of
                          each step (reference.py:58); zeroed by the call */
+  long long* phase_ns; /* [min(steps, IPC_NET_TRACE_STEPS), IPC_NET_TRACE_PHASES] or NULL:
+                          %globaltimer stamps (ns) taken by CTA 0 of network 0 at the end of
+                          each phase of a step (tracing; no work is skipped) */
 } ipc_net_run_t;
+
+#define IPC_NET_TRACE_STEPS 64
+#define IPC_NET_TRACE_PHASES 12 /* start, mu-partial, barrier A, mu-sum, forward, iterations,
+                                   energy, barrier B, input-layer update, hidden updates,
+                                   batch ready, end */
 
 /* Whether ipc_net_train can run this network: IPC_OK and the cluster size
  * (CTAs per network) and dynamic shared memory per CTA it would use, or an

@@ -29,6 +29,8 @@ DTYPE_NAMES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": t
 ALGO_CODES = {"auto": 0, "simt": 1, "generic": 1, "tcgen05": 2, "outer": 3}
 
 NET_MAX_LAYERS = 8
+NET_TRACE_STEPS = 64
+NET_TRACE_PHASES = 12
 
 EXPORTED = (
     "ipc_abi_version", "ipc_last_error", "ipc_launch_count", "ipc_pred_err", "ipc_pred_err_saved",
@@ -66,6 +68,7 @@ class IpcNetRun(Structure):
         ("dtype", c_int),
         ("cluster", c_int),
         ("energy", c_void_p),
+        ("phase_ns", c_void_p),
     ]
 
 

@@ -63,6 +63,60 @@ __device__ __forceinline__ float act_df(float x) {
 }
 
 // ---------------------------------------------------------------------------
+// Hardware-approximate activations for 16-bit storage.  tanh.approx.f32 and
+// ex2.approx.f32 are single MUFU instructions with a relative error near
+// 2^-11, the size of one fp16 rounding step, so on the 16-bit path they move
+// results by about one storage ulp.  The fp32 path always uses the accurate
+// forms above.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float tanh_hw(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float sigmoid_hw(float x) {
+  // 1 / (1 + 2^(-x log2 e)), exponent and reciprocal on the MUFU unit
+  float t, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(-1.4426950408889634f * x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + t));
+  return r;
+}
+
+template <int ACT>
+__device__ __forceinline__ float act_f_hw(float x) {
+  if constexpr (ACT == IPC_ACT_TANH) {
+    return tanh_hw(x);
+  } else if constexpr (ACT == IPC_ACT_SIGMOID) {
+    return sigmoid_hw(x);
+  } else if constexpr (ACT == IPC_ACT_SILU) {
+    return x * sigmoid_hw(x);
+  } else if constexpr (ACT == IPC_ACT_GELU) {
+    return 0.5f * x * (1.f + tanh_hw(kGeluK * (x + kGeluC * x * x * x)));
+  } else {
+    return act_f<ACT>(x);
+  }
+}
+
+template <int ACT>
+__device__ __forceinline__ float act_df_hw(float x) {
+  if constexpr (ACT == IPC_ACT_TANH) {
+    const float y = tanh_hw(x);
+    return 1.f - y * y;
+  } else if constexpr (ACT == IPC_ACT_SIGMOID) {
+    const float y = sigmoid_hw(x);
+    return y * (1.f - y);
+  } else if constexpr (ACT == IPC_ACT_SILU) {
+    const float s = sigmoid_hw(x);
+    return s * (1.f + x * (1.f - s));
+  } else if constexpr (ACT == IPC_ACT_GELU) {
+    const float t = tanh_hw(kGeluK * (x + kGeluC * x * x * x));
+    return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * kGeluK * (1.f + 3.f * kGeluC * x * x);
+  } else {
+    return act_df<ACT>(x);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Storage types.
 // ---------------------------------------------------------------------------
 template <typename T>

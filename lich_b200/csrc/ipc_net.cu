@@ -23,13 +23,20 @@
 //    for a training step (W and x_L do not change inside it), so it is
 //    computed once and reused by the forward sweep and all T prediction
 //    passes -- the same number the reference recomputes T+1 times.
-//  * Weight update (reduction over all B columns): after a cluster barrier
-//    each CTA gathers, over DSMEM, the rows of E and f(x) its share of the
-//    output tiles needs, updates its input-layer slice in place and its share
-//    of every hidden W, and writes the new hidden tiles into every CTA's
-//    replica.  The next step's batch is prefetched with cp.async meanwhile.
+//  * Weight update (a reduction over all B columns): every CTA *pushes* its
+//    columns of e[L-1] to all CTAs and its columns of e[l], f(x[l+1]) to the
+//    CTA that owns hidden layer l (l mod C); after one cluster barrier each
+//    CTA updates its input-layer slice and its hidden layer(s) from local
+//    shared memory and stores the new hidden weights into every replica.
+//    The exchange is DSMEM stores only (no remote loads, so no round-trip
+//    latency on the critical path); the next batch is prefetched with
+//    cp.async while the update runs.
 //  * Two cluster barriers per training step; global memory is touched only
 //    for the batch (read once) and the outputs at the end of the launch.
+//
+// Shared-memory state tiles are [rows][NCOL] with the 16-byte chunks of each
+// row XOR-swizzled by row, so ldmatrix reads of 8 consecutive rows hit 8
+// distinct bank groups without padding.
 //
 // Tensor cores: mma.sync m16n8k16 with fp32 accumulators, fragments from
 // shared memory via ldmatrix.  Every GEMM here is a handful of 16x8x16 tiles
@@ -40,6 +47,7 @@
 // (tilelang_kernels.py:163), e = cast(x) - cast(acc) (:173),
 // x = cast(x + g(-e + f'(x) acc)) (:229-230), W = cast(W + a acc) (:320), and
 // the forward sweep x[l] = cast(W[l] @ f(x[l+1])) (trainer.py:513-515).
+// f and f' use the MUFU approximations of ipc_common.cuh (16-bit storage).
 #include <cstdio>
 
 #include "ipc_common.cuh"
@@ -47,16 +55,17 @@
 namespace ipc {
 namespace {
 
-constexpr int NET_THREADS = 256;
+constexpr int NET_THREADS = 512;
 constexpr int NET_WARPS = NET_THREADS / 32;
 constexpr int WLD = 72;  // smem row stride (elements) of replicated hidden W tiles (<= 64 cols + 8)
 constexpr int MAXL = IPC_NET_MAX_LAYERS;
 constexpr int MAX_CLUSTER = 8;
+constexpr int MAX_OWN = MAXL;  // hidden layers owned per CTA
 constexpr int SMEM_LIMIT = 227 * 1024;
 
 template <typename T>
 struct NetParams {
-  int L, B, nets, C, KS, KSP;  // KS: input-layer K slice per CTA (multiple of 8), KSP = KS rounded to 16
+  int L, B, nets, C, KS, KSP, nown;  // KS: input-layer K slice per CTA (multiple of 8), KSP = KS rounded to 16
   int dims[MAXL + 1];
   int rows16[MAXL + 1];
   T* w[MAXL];
@@ -67,10 +76,12 @@ struct NetParams {
   int pool_batches, first_batch, steps, T_it, forward_init, update_weights;
   float alpha, gamma;
   float* energy;
+  long long* phase_ns;
   // shared-memory layout, byte offsets
   int o_w[MAXL], o_x[MAXL], o_a[MAXL], o_e[MAXL];
-  int o_wt, o_al, o_recv, o_ge, o_ga, o_mu;
-  int sld, wtld, ald, gld;
+  int o_ge[MAX_OWN], o_ga[MAX_OWN];
+  int o_mu, o_wt, o_al, o_recv, o_gt;
+  int wtld, ald, gld;
   int smem_bytes;
 };
 
@@ -109,6 +120,62 @@ __device__ __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint3
   }
 }
 
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_dsmem_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void st_dsmem_f2(uint32_t addr, float a, float b) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1,%2};\n" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+__device__ __forceinline__ void st_dsmem_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_dsmem_u16(uint32_t addr, uint16_t v) {
+  asm volatile("st.shared::cluster.u16 [%0], %1;\n" ::"r"(addr), "h"(v) : "memory");
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+__device__ __forceinline__ long long globaltimer_ns() {
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+
+template <typename T>
+__device__ __forceinline__ uint16_t bits(float v) {
+  T h = St<T>::st(v);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+template <typename T>
+__device__ __forceinline__ uint32_t bits2(float a, float b) {
+  return (uint32_t)bits<T>(a) | ((uint32_t)bits<T>(b) << 16);
+}
+template <typename T>
+__device__ __forceinline__ void unpack2(uint32_t v, float& a, float& b) {
+  const uint16_t lo = v & 0xffffu, hi = v >> 16;
+  a = St<T>::ld(*reinterpret_cast<const T*>(&lo));
+  b = St<T>::ld(*reinterpret_cast<const T*>(&hi));
+}
+
+// Element offset of (row r, column c) in a swizzled [rows][NCOL] state tile:
+// 16-byte chunk j of row r is stored at chunk j ^ s(r).
+template <int NCOL>
+__device__ __forceinline__ int sw(int r, int c) {
+  constexpr int VPR = NCOL / 8;
+  const int s = ((r * VPR) >> 3) & (VPR - 1);
+  return r * NCOL + ((((c >> 3) ^ s)) << 3) + (c & 7);
+}
+
 // A fragment (16x16) from row-major [m][k] shared memory (ld in elements).
 __device__ __forceinline__ void frag_a(uint32_t (&r)[4], uint32_t base, int ld, int m0, int k0, int lane) {
   const int q = lane >> 3, j = lane & 7;
@@ -119,10 +186,16 @@ __device__ __forceinline__ void frag_a_t(uint32_t (&r)[4], uint32_t base, int ld
   const int q = lane >> 3, j = lane & 7;
   ldsm_x4_t(r, base + 2 * ((k0 + j + (q >> 1) * 8) * ld + m0 + (q & 1) * 8));
 }
-// B fragment (16x8) from row-major [k][n].
+// B fragment (16x8) from row-major [k][n] (plain layout).
 __device__ __forceinline__ void frag_b_kn(uint32_t (&r)[2], uint32_t base, int ld, int k0, int n0, int lane) {
   const int q = (lane >> 3) & 1, j = lane & 7;
   ldsm_x2_t(r, base + 2 * ((k0 + j + q * 8) * ld + n0));
+}
+// B fragment (16x8) from a swizzled state tile [k][NCOL].
+template <int NCOL>
+__device__ __forceinline__ void frag_b_sw(uint32_t (&r)[2], uint32_t base, int k0, int n0, int lane) {
+  const int q = (lane >> 3) & 1, j = lane & 7;
+  ldsm_x2_t(r, base + 2 * sw<NCOL>(k0 + j + q * 8, n0));
 }
 // B fragment (16x8) from row-major [n][k].
 __device__ __forceinline__ void frag_b_nk(uint32_t (&r)[2], uint32_t base, int ld, int k0, int n0, int lane) {
@@ -130,104 +203,34 @@ __device__ __forceinline__ void frag_b_nk(uint32_t (&r)[2], uint32_t base, int l
   ldsm_x2(r, base + 2 * ((n0 + j) * ld + k0 + q * 8));
 }
 
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-}
-__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ uint4 ld_dsmem16(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared::cluster.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_dsmem_f2(uint32_t addr, float a, float b) {
-  asm volatile("st.shared::cluster.v2.f32 [%0], {%1,%2};\n" ::"r"(addr), "f"(a), "f"(b) : "memory");
-}
-__device__ __forceinline__ void st_dsmem_u16(uint32_t addr, uint16_t v) {
-  asm volatile("st.shared::cluster.u16 [%0], %1;\n" ::"r"(addr), "h"(v) : "memory");
-}
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
-
-template <typename T>
-__device__ __forceinline__ uint16_t bits(float v) {
-  T h = St<T>::st(v);
-  return *reinterpret_cast<uint16_t*>(&h);
-}
-template <typename T>
-__device__ __forceinline__ T& at(uint8_t* smem, int off, int idx) {
-  return reinterpret_cast<T*>(smem + off)[idx];
-}
-
 // --------------------------------------------------------- kernel helpers
-// Copy rows [0, rows) x cols [c0, c0+ncol) of a row-major global matrix (ld
-// gld) into shared memory (ld sld, 16-byte rows); ncol multiple of 8.
+// cp.async rows [0, rows) x columns [0, ncol) of a row-major global matrix
+// (ld gld) into a plain shared array (ld sld); ncol multiple of 8.
 template <typename T>
-__device__ __forceinline__ void async_rows(uint8_t* smem, int off, int sld, const T* g, long long gld, int rows,
-                                           int c0, int ncol) {
+__device__ __forceinline__ void async_plain(uint8_t* smem, int off, int sld, const T* g, long long gld, int rows,
+                                            int ncol) {
   const int vpr = ncol / 8;
   for (int it = threadIdx.x; it < rows * vpr; it += NET_THREADS) {
     const int r = it / vpr, c = (it % vpr) * 8;
-    cp_async16(smem_addr(smem + off) + 2 * (r * sld + c), g + (long long)r * gld + c0 + c);
+    cp_async16(smem_addr(smem + off) + 2 * (r * sld + c), g + (long long)r * gld + c);
   }
 }
-
-// f applied in place to rows [0, rows) x cols [0, ncol) of a shared array.
-template <typename T, int ACT>
-__device__ __forceinline__ void act_inplace(uint8_t* smem, int off, int sld, int rows, int ncol) {
-  for (int it = threadIdx.x; it < rows * ncol; it += NET_THREADS) {
-    T& v = at<T>(smem, off, (it / ncol) * sld + it % ncol);
-    v = St<T>::st(act_f<ACT>(St<T>::ld(v)));
-  }
-}
-// a[l] = cast(f(x[l])) over the valid rows of the CTA's columns.
-template <typename T, int ACT, int NCOL>
-__device__ __forceinline__ void act_rows(uint8_t* smem, const NetParams<T>& p, int l) {
-  for (int it = threadIdx.x; it < p.dims[l] * NCOL; it += NET_THREADS) {
-    const int i = (it / NCOL) * p.sld + it % NCOL;
-    at<T>(smem, p.o_a[l], i) = St<T>::st(act_f<ACT>(St<T>::ld(at<T>(smem, p.o_x[l], i))));
-  }
-}
-
-// Gather rows [r0, r1) of a state array (offset `off`, ld sld) for ALL batch
-// columns from every CTA of the cluster into a local [r1-r0][gld] buffer.
-template <int NCOL>
-__device__ __forceinline__ void gather_rows(uint8_t* smem, int dst_off, int gld, int src_off, int sld, int r0, int r1,
-                                            int C) {
-  constexpr int VPR = NCOL / 8;  // 16-byte vectors per source row
-  const int per_row = C * VPR;
-  const int n = (r1 - r0) * per_row;
-  const uint32_t src_base = smem_addr(smem + src_off);
-  for (int base = threadIdx.x; base < n; base += 4 * NET_THREADS) {
-    uint4 v[4];
-    int dst[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int it = base + u * NET_THREADS;
-      dst[u] = -1;
-      if (it < n) {
-        const int r = it / per_row, rem = it % per_row;
-        const int cc = rem / VPR, j = rem % VPR;
-        v[u] = ld_dsmem16(mapa(src_base + 2 * ((r0 + r) * sld + j * 8), cc));
-        dst[u] = 2 * (r * gld + cc * NCOL + j * 8);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-      if (dst[u] >= 0) *reinterpret_cast<uint4*>(smem + dst_off + dst[u]) = v[u];
+// cp.async rows [0, rows) x the CTA's NCOL columns (starting at c0) into a swizzled state tile.
+template <typename T, int NCOL>
+__device__ __forceinline__ void async_state(uint8_t* smem, int off, const T* g, long long gld, int rows, int c0) {
+  constexpr int VPR = NCOL / 8;
+  for (int it = threadIdx.x; it < rows * VPR; it += NET_THREADS) {
+    const int r = it / VPR, c = (it % VPR) * 8;
+    cp_async16(smem_addr(smem + off) + 2 * sw<NCOL>(r, c), g + (long long)r * gld + c0 + c);
   }
 }
 
 template <typename T, int ACT, int NCOL>
-__global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_constant__ NetParams<T> p) {
+__global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_constant__ NetParams<T> p) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const int cta = blockIdx.x;  // == %cluster_ctarank: the cluster spans gridDim.x
+  constexpr int NT = NCOL / 8;   // n8 tiles per CTA column block
+  constexpr int VPR = NCOL / 8;  // 16-byte chunks per state row
+  const int cta = blockIdx.x;    // == %cluster_ctarank: the cluster spans gridDim.x
   const int net = blockIdx.y;
   const int C = p.C;
   const int c0 = cta * NCOL;
@@ -235,10 +238,17 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_consta
   const int gq = lane >> 2, tq = lane & 3;
   const int L = p.L, Lt = L - 1, B = p.B;
   const int dL = p.dims[L], dT = p.dims[Lt];
-  const int SLD = p.sld;
+  const int B16 = ((B + 15) / 16) * 16;
   const int k_lo = cta * p.KS;
   const int kcnt = max(0, min(p.KS, dL - k_lo));  // input-layer K rows owned by this CTA
   const uint32_t sbase = smem_addr(smem);
+  auto S = [&](int off) { return reinterpret_cast<T*>(smem + off); };
+  auto U32 = [&](int off, int elem) -> uint32_t& { return *reinterpret_cast<uint32_t*>(smem + off + 2 * elem); };
+
+  const bool tracer = p.phase_ns != nullptr && net == 0 && cta == 0 && threadIdx.x == 0;
+  auto trace = [&](int step, int phase) {
+    if (tracer && step < IPC_NET_TRACE_STEPS) p.phase_ns[step * IPC_NET_TRACE_PHASES + phase] = globaltimer_ns();
+  };
 
   // zero everything once: padding rows / columns of every operand stay zero
   for (int i = threadIdx.x; i < p.smem_bytes / 16; i += NET_THREADS)
@@ -259,39 +269,61 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_consta
     const int b = (p.first_batch + step) % p.pool_batches;
     return p.pool_y + ((long long)b * p.nets + net) * (long long)p.dims[0] * B;
   };
+  // f over the owned K rows of the batch, all columns (plain [KSP][ald] tile)
+  auto activate_batch = [&]() {
+    for (int it = threadIdx.x; it < kcnt * (B / 2); it += NET_THREADS) {
+      const int r = it / (B / 2), c = (it % (B / 2)) * 2;
+      uint32_t& v = U32(p.o_al, r * p.ald + c);
+      float a, b;
+      unpack2<T>(v, a, b);
+      v = bits2<T>(act_f_hw<ACT>(a), act_f_hw<ACT>(b));
+    }
+  };
+  // a[l] = cast(f(x[l])) over the valid rows of the CTA's columns
+  auto act_rows = [&](int l) {
+    for (int it = threadIdx.x; it < p.dims[l] * (NCOL / 2); it += NET_THREADS) {
+      const int r = it / (NCOL / 2), c = (it % (NCOL / 2)) * 2;
+      float a, b;
+      unpack2<T>(U32(p.o_x[l], sw<NCOL>(r, c)), a, b);
+      U32(p.o_a[l], sw<NCOL>(r, c)) = bits2<T>(act_f_hw<ACT>(a), act_f_hw<ACT>(b));
+    }
+  };
 
   // ---- resident weights: hidden replicas and this CTA's input-layer slice ----
   for (int l = 0; l < Lt; ++l) {
     const int cols = p.dims[l + 1];
+    const T* src = gw(l);
     for (int it = threadIdx.x; it < p.dims[l] * cols; it += NET_THREADS)
-      at<T>(smem, p.o_w[l], (it / cols) * WLD + it % cols) = gw(l)[it];
+      S(p.o_w[l])[(it / cols) * WLD + it % cols] = src[it];
   }
-  for (int it = threadIdx.x; it < dT * kcnt; it += NET_THREADS) {
-    const int r = it / kcnt, k = it % kcnt;
-    at<T>(smem, p.o_wt, r * p.wtld + k) = gw(Lt)[(long long)r * dL + k_lo + k];
+  {
+    const T* src = gw(Lt);
+    for (int it = threadIdx.x; it < dT * kcnt; it += NET_THREADS) {
+      const int r = it / kcnt, k = it % kcnt;
+      S(p.o_wt)[r * p.wtld + k] = src[(long long)r * dL + k_lo + k];
+    }
   }
-  // ---- first batch: f(x_L) for the owned K rows (all columns), targets for the owned columns ----
-  async_rows<T>(smem, p.o_al, p.ald, batch_x(0) + (long long)k_lo * B, B, kcnt, 0, B);
-  async_rows<T>(smem, p.o_x[0], SLD, batch_y(0), B, p.dims[0], c0, NCOL);
+  // ---- first batch: owned K rows of x_L (all columns), targets of the owned columns ----
+  async_plain<T>(smem, p.o_al, p.ald, batch_x(0) + (long long)k_lo * B, B, kcnt, B);
+  async_state<T, NCOL>(smem, p.o_x[0], batch_y(0), B, p.dims[0], c0);
   if (!p.forward_init)
-    for (int l = 1; l <= Lt; ++l) async_rows<T>(smem, p.o_x[l], SLD, gx(l), B, p.dims[l], c0, NCOL);
+    for (int l = 1; l <= Lt; ++l) async_state<T, NCOL>(smem, p.o_x[l], gx(l), B, p.dims[l], c0);
   cp_async_wait_all();
   __syncthreads();
-  act_inplace<T, ACT>(smem, p.o_al, p.ald, kcnt, B);
+  activate_batch();
   if (!p.forward_init)
-    for (int l = 1; l <= Lt; ++l) act_rows<T, ACT, NCOL>(smem, p, l);
+    for (int l = 1; l <= Lt; ++l) act_rows(l);
   __syncthreads();
 
   const uint32_t recv_base = sbase + p.o_recv;
 
   for (int step = 0; step < p.steps; ++step) {
+    trace(step, 0);
     if (!p.update_weights && step > 0) cluster_sync_all();  // peers done with their receive buffers
 
     // ---- mu partial: W[L-1][:, own K] f(x_L)[own K, all columns] -> owner CTAs ----
     {
-      const int mtiles = p.rows16[Lt] / 16;
-      const int ntiles = B / 8;
-      const int ksteps = (kcnt + 15) / 16;
+      const int mtiles = p.rows16[Lt] / 16, ntiles = B / 8, ksteps = (kcnt + 15) / 16;
       for (int u = warp; u < mtiles * ntiles; u += NET_WARPS) {
         const int mt = u / ntiles, nt = u % ntiles;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -308,31 +340,38 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_consta
         st_dsmem_f2(dst + 4 * 8 * NCOL, acc[2], acc[3]);
       }
     }
-    cluster_sync_all();  // (A) partials delivered; every peer finished reading last step's e / f(x)
+    trace(step, 1);
+    cluster_sync_all();  // (A) partials delivered; every peer finished with last step's pushes / broadcasts
+    trace(step, 2);
 
     // ---- mu for the owned columns: sum of the C partials in a fixed order ----
-    for (int it = threadIdx.x; it < p.rows16[Lt] * NCOL; it += NET_THREADS) {
-      const int r = it / NCOL, j = it % NCOL;
-      float s = 0.f;
-      for (int cc = 0; cc < C; ++cc)
-        s += reinterpret_cast<const float*>(smem + p.o_recv)[(cc * p.rows16[Lt] + r) * NCOL + j];
-      at<T>(smem, p.o_mu, r * SLD + j) = St<T>::st(r < dT ? s : 0.f);
+    for (int it = threadIdx.x; it < p.rows16[Lt] * (NCOL / 2); it += NET_THREADS) {
+      const int r = it / (NCOL / 2), j = (it % (NCOL / 2)) * 2;
+      float s0 = 0.f, s1 = 0.f;
+      for (int cc = 0; cc < C; ++cc) {
+        const float2 v = reinterpret_cast<const float2*>(smem + p.o_recv)[((cc * p.rows16[Lt] + r) * NCOL + j) / 2];
+        s0 += v.x;
+        s1 += v.y;
+      }
+      U32(p.o_mu, sw<NCOL>(r, j)) = r < dT ? bits2<T>(s0, s1) : 0u;
     }
     __syncthreads();
+    trace(step, 3);
 
     // ---- forward-init sweep: x[L-1] = cast(mu), x[l] = cast(W[l] f(x[l+1])) ----
     if (p.forward_init) {
       if (Lt >= 1) {
-        for (int it = threadIdx.x; it < dT * NCOL; it += NET_THREADS) {
-          const int i = (it / NCOL) * SLD + it % NCOL;
-          at<T>(smem, p.o_x[Lt], i) = at<T>(smem, p.o_mu, i);
+        for (int it = threadIdx.x; it < dT * (NCOL / 2); it += NET_THREADS) {
+          const int r = it / (NCOL / 2), c = (it % (NCOL / 2)) * 2;
+          const uint32_t v = U32(p.o_mu, sw<NCOL>(r, c));
+          float a, b;
+          unpack2<T>(v, a, b);
+          U32(p.o_x[Lt], sw<NCOL>(r, c)) = v;
+          U32(p.o_a[Lt], sw<NCOL>(r, c)) = bits2<T>(act_f_hw<ACT>(a), act_f_hw<ACT>(b));
         }
-        __syncthreads();
-        act_rows<T, ACT, NCOL>(smem, p, Lt);
         __syncthreads();
       }
       for (int l = Lt - 1; l >= 1; --l) {
-        constexpr int NT = NCOL / 8;
         const int mtiles = p.rows16[l] / 16, ksteps = p.rows16[l + 1] / 16;
         for (int u = warp; u < mtiles * NT; u += NET_WARPS) {
           const int mt = u / NT, nt = u % NT;
@@ -340,27 +379,26 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_consta
           for (int ks = 0; ks < ksteps; ++ks) {
             uint32_t af[4], bf[2];
             frag_a(af, sbase + p.o_w[l], WLD, mt * 16, ks * 16, lane);
-            frag_b_kn(bf, sbase + p.o_a[l + 1], SLD, ks * 16, nt * 8, lane);
+            frag_b_sw<NCOL>(bf, sbase + p.o_a[l + 1], ks * 16, nt * 8, lane);
             mma<T>(acc, af, bf[0], bf[1]);
           }
-          const int r = mt * 16 + gq, c = nt * 8 + 2 * tq;
+          const int c = nt * 8 + 2 * tq;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int rr = r + 8 * h;
+            const int rr = mt * 16 + gq + 8 * h;
             if (rr >= p.dims[l]) continue;
-            at<T>(smem, p.o_x[l], rr * SLD + c) = St<T>::st(acc[2 * h]);
-            at<T>(smem, p.o_x[l], rr * SLD + c + 1) = St<T>::st(acc[2 * h + 1]);
-            at<T>(smem, p.o_a[l], rr * SLD + c) = St<T>::st(act_f<ACT>(rnd<T>(acc[2 * h])));
-            at<T>(smem, p.o_a[l], rr * SLD + c + 1) = St<T>::st(act_f<ACT>(rnd<T>(acc[2 * h + 1])));
+            U32(p.o_x[l], sw<NCOL>(rr, c)) = bits2<T>(acc[2 * h], acc[2 * h + 1]);
+            U32(p.o_a[l], sw<NCOL>(rr, c)) =
+                bits2<T>(act_f_hw<ACT>(rnd<T>(acc[2 * h])), act_f_hw<ACT>(rnd<T>(acc[2 * h + 1])));
           }
         }
         __syncthreads();
       }
     }
+    trace(step, 4);
 
     // ---- T inference iterations ----
     for (int t = 0; t < p.T_it; ++t) {
-      constexpr int NT = NCOL / 8;
       // P: e[l] = cast(x[l]) - cast(W[l] f(x[l+1])), l < L-1 on tensor cores; the input layer uses mu
       {
         int base = 0;
@@ -372,27 +410,29 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_consta
             for (int ks = 0; ks < ksteps; ++ks) {
               uint32_t af[4], bf[2];
               frag_a(af, sbase + p.o_w[l], WLD, mt * 16, ks * 16, lane);
-              frag_b_kn(bf, sbase + p.o_a[l + 1], SLD, ks * 16, nt * 8, lane);
+              frag_b_sw<NCOL>(bf, sbase + p.o_a[l + 1], ks * 16, nt * 8, lane);
               mma<T>(acc, af, bf[0], bf[1]);
             }
-            const int r = mt * 16 + gq, c = nt * 8 + 2 * tq;
+            const int c = nt * 8 + 2 * tq;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int rr = r + 8 * h;
+              const int rr = mt * 16 + gq + 8 * h;
               if (rr >= p.dims[l]) continue;
-#pragma unroll
-              for (int j = 0; j < 2; ++j) {
-                const int i = rr * SLD + c + j;
-                at<T>(smem, p.o_e[l], i) = St<T>::st(St<T>::ld(at<T>(smem, p.o_x[l], i)) - rnd<T>(acc[2 * h + j]));
-              }
+              const int i = sw<NCOL>(rr, c);
+              float xa, xb;
+              unpack2<T>(U32(p.o_x[l], i), xa, xb);
+              U32(p.o_e[l], i) = bits2<T>(xa - rnd<T>(acc[2 * h]), xb - rnd<T>(acc[2 * h + 1]));
             }
           }
           base += units;
         }
-        for (int it = threadIdx.x; it < dT * NCOL; it += NET_THREADS) {
-          const int i = (it / NCOL) * SLD + it % NCOL;
-          at<T>(smem, p.o_e[Lt], i) =
-              St<T>::st(St<T>::ld(at<T>(smem, p.o_x[Lt], i)) - St<T>::ld(at<T>(smem, p.o_mu, i)));
+        for (int it = threadIdx.x; it < dT * (NCOL / 2); it += NET_THREADS) {
+          const int r = it / (NCOL / 2), c = (it % (NCOL / 2)) * 2;
+          const int i = sw<NCOL>(r, c);
+          float xa, xb, ma, mb;
+          unpack2<T>(U32(p.o_x[Lt], i), xa, xb);
+          unpack2<T>(U32(p.o_mu, i), ma, mb);
+          U32(p.o_e[Lt], i) = bits2<T>(xa - ma, xb - mb);
         }
       }
       __syncthreads();
@@ -407,23 +447,22 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_consta
             for (int ks = 0; ks < ksteps; ++ks) {
               uint32_t af[4], bf[2];
               frag_a_t(af, sbase + p.o_w[l - 1], WLD, mt * 16, ks * 16, lane);
-              frag_b_kn(bf, sbase + p.o_e[l - 1], SLD, ks * 16, nt * 8, lane);
+              frag_b_sw<NCOL>(bf, sbase + p.o_e[l - 1], ks * 16, nt * 8, lane);
               mma<T>(acc, af, bf[0], bf[1]);
             }
-            const int r = mt * 16 + gq, c = nt * 8 + 2 * tq;
+            const int c = nt * 8 + 2 * tq;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int rr = r + 8 * h;
+              const int rr = mt * 16 + gq + 8 * h;
               if (rr >= p.dims[l]) continue;
+              const int i = sw<NCOL>(rr, c);
+              float xv[2], ev[2], xn[2];
+              unpack2<T>(U32(p.o_x[l], i), xv[0], xv[1]);
+              unpack2<T>(U32(p.o_e[l], i), ev[0], ev[1]);
 #pragma unroll
-              for (int j = 0; j < 2; ++j) {
-                const int i = rr * SLD + c + j;
-                const float xv = St<T>::ld(at<T>(smem, p.o_x[l], i));
-                const float ev = St<T>::ld(at<T>(smem, p.o_e[l], i));
-                const float xn = xv + p.gamma * (-ev + act_df<ACT>(xv) * acc[2 * h + j]);
-                at<T>(smem, p.o_x[l], i) = St<T>::st(xn);
-                at<T>(smem, p.o_a[l], i) = St<T>::st(act_f<ACT>(rnd<T>(xn)));
-              }
+              for (int j = 0; j < 2; ++j) xn[j] = xv[j] + p.gamma * (-ev[j] + act_df_hw<ACT>(xv[j]) * acc[2 * h + j]);
+              U32(p.o_x[l], i) = bits2<T>(xn[0], xn[1]);
+              U32(p.o_a[l], i) = bits2<T>(act_f_hw<ACT>(rnd<T>(xn[0])), act_f_hw<ACT>(rnd<T>(xn[1])));
             }
           }
           base += units;
@@ -431,6 +470,7 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_consta
       }
       __syncthreads();
     }
+    trace(step, 5);
 
     // ---- energy of the last iteration: sum_l mean(e[l]^2) (reference.py:58) ----
     if (p.energy != nullptr) {
@@ -438,7 +478,7 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_consta
       for (int l = 0; l <= Lt; ++l) {
         float sl = 0.f;
         for (int it = threadIdx.x; it < p.dims[l] * NCOL; it += NET_THREADS) {
-          const float v = St<T>::ld(at<T>(smem, p.o_e[l], (it / NCOL) * SLD + it % NCOL));
+          const float v = St<T>::ld(S(p.o_e[l])[sw<NCOL>(it / NCOL, it % NCOL)]);
           sl = fmaf(v, v, sl);
         }
         part += sl / ((float)p.dims[l] * (float)B);
@@ -447,14 +487,36 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_consta
       for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
       if (lane == 0) atomicAdd(p.energy + (long long)step * p.nets + net, part);
     }
+    trace(step, 6);
 
     const bool more = step + 1 < p.steps;
     if (p.update_weights) {
-      cluster_sync_all();  // (B) every CTA's e / f(x) of this step are final
-      const int B16 = ((B + 15) / 16) * 16;
-      // ---- input layer: W[L-1][:, own K] += alpha E[L-1] f(x_L)^T  (local slice) ----
-      gather_rows<NCOL>(smem, p.o_ge, p.gld, p.o_e[Lt], SLD, 0, p.rows16[Lt], C);
-      __syncthreads();
+      // ---- push the weight-update operands (DSMEM stores only) ----
+      {
+        // e[L-1], owned columns -> every CTA's E_top[:, c0 .. c0+NCOL)
+        const int n_top = p.rows16[Lt] * VPR;
+        for (int it = threadIdx.x; it < n_top * C; it += NET_THREADS) {
+          const int cc = it / n_top, rem = it % n_top, r = rem / VPR, j = rem % VPR;
+          const uint4 v = *reinterpret_cast<const uint4*>(smem + p.o_e[Lt] + 2 * sw<NCOL>(r, 8 * j));
+          st_dsmem_v4(mapa(sbase + p.o_gt + 2 * (r * p.gld + c0 + 8 * j), cc), v);
+        }
+        // e[l], f(x[l+1]) owned columns -> the CTA owning hidden layer l
+        for (int l = 0; l < Lt; ++l) {
+          const int owner = l % C, slot = l / C;
+          const int ne = p.rows16[l] * VPR, na = p.rows16[l + 1] * VPR;
+          for (int it = threadIdx.x; it < ne + na; it += NET_THREADS) {
+            const bool isE = it < ne;
+            const int rem = isE ? it : it - ne, r = rem / VPR, j = rem % VPR;
+            const int src_off = isE ? p.o_e[l] : p.o_a[l + 1];
+            const int dst_off = isE ? p.o_ge[slot] : p.o_ga[slot];
+            const uint4 v = *reinterpret_cast<const uint4*>(smem + src_off + 2 * sw<NCOL>(r, 8 * j));
+            st_dsmem_v4(mapa(sbase + dst_off + 2 * (r * p.gld + c0 + 8 * j), owner), v);
+          }
+        }
+      }
+      cluster_sync_all();  // (B) every CTA holds the operands of the layers it updates
+      trace(step, 7);
+      // ---- input layer: W[L-1][:, own K] += alpha E[L-1] f(x_L)^T (local slice) ----
       {
         const int mtiles = p.rows16[Lt] / 16, ntiles = p.KSP / 8;
         for (int u = warp; u < mtiles * ntiles; u += NET_WARPS) {
@@ -463,109 +525,108 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_consta
           float acc[4] = {0.f, 0.f, 0.f, 0.f};
           for (int b0 = 0; b0 < B16; b0 += 16) {
             uint32_t af[4], bf[2];
-            frag_a(af, sbase + p.o_ge, p.gld, mt * 16, b0, lane);
+            frag_a(af, sbase + p.o_gt, p.gld, mt * 16, b0, lane);
             frag_b_nk(bf, sbase + p.o_al, p.ald, b0, nt * 8, lane);
             mma<T>(acc, af, bf[0], bf[1]);
           }
-          const int r = mt * 16 + gq, k = nt * 8 + 2 * tq;
+          const int k = nt * 8 + 2 * tq;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int rr = r + 8 * h;
+            const int rr = mt * 16 + gq + 8 * h;
             if (rr >= dT) continue;
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
               if (k + j >= kcnt) continue;
-              T& wv = at<T>(smem, p.o_wt, rr * p.wtld + k + j);
+              T& wv = S(p.o_wt)[rr * p.wtld + k + j];
               wv = St<T>::st(St<T>::ld(wv) + p.alpha * acc[2 * h + j]);
             }
           }
         }
       }
       __syncthreads();  // f(x_L) of this step no longer needed
+      trace(step, 8);
       if (more) {
-        async_rows<T>(smem, p.o_al, p.ald, batch_x(step + 1) + (long long)k_lo * B, B, kcnt, 0, B);
-        async_rows<T>(smem, p.o_x[0], SLD, batch_y(step + 1), B, p.dims[0], c0, NCOL);
+        async_plain<T>(smem, p.o_al, p.ald, batch_x(step + 1) + (long long)k_lo * B, B, kcnt, B);
+        async_state<T, NCOL>(smem, p.o_x[0], batch_y(step + 1), B, p.dims[0], c0);
       }
-      // ---- hidden layers: this CTA's share of the 16x8 output tiles, written to every replica ----
-      for (int l = 0; l < Lt; ++l) {
-        const int ntl = p.rows16[l + 1] / 8, mtl = p.rows16[l] / 16, U = mtl * ntl;
-        const int u0 = (cta * U) / C, u1 = ((cta + 1) * U) / C;
-        if (u0 >= u1) continue;  // uniform across the CTA
-        const int mt_lo = u0 / ntl, mt_hi = (u1 - 1) / ntl;
-        const int nt_lo = (mt_lo == mt_hi) ? u0 % ntl : 0;
-        const int nt_hi = (mt_lo == mt_hi) ? (u1 - 1) % ntl : ntl - 1;
-        __syncthreads();  // staging free
-        gather_rows<NCOL>(smem, p.o_ge, p.gld, p.o_e[l], SLD, mt_lo * 16, mt_hi * 16 + 16, C);
-        gather_rows<NCOL>(smem, p.o_ga, p.gld, p.o_a[l + 1], SLD, nt_lo * 8, nt_hi * 8 + 8, C);
-        __syncthreads();
+      // ---- owned hidden layers: full reduction over B, new tiles stored into every replica ----
+      for (int slot = 0; slot < p.nown; ++slot) {
+        const int l = cta + slot * C;
+        if (l >= Lt) break;
         const int cols = p.dims[l + 1];
-        for (int u = u0 + warp; u < u1; u += NET_WARPS) {
+        const int mtl = p.rows16[l] / 16, ntl = p.rows16[l + 1] / 8;
+        for (int u = warp; u < mtl * ntl; u += NET_WARPS) {
           const int mt = u / ntl, nt = u % ntl;
           float acc[4] = {0.f, 0.f, 0.f, 0.f};
           for (int b0 = 0; b0 < B16; b0 += 16) {
             uint32_t af[4], bf[2];
-            frag_a(af, sbase + p.o_ge, p.gld, (mt - mt_lo) * 16, b0, lane);
-            frag_b_nk(bf, sbase + p.o_ga, p.gld, b0, (nt - nt_lo) * 8, lane);
+            frag_a(af, sbase + p.o_ge[slot], p.gld, mt * 16, b0, lane);
+            frag_b_nk(bf, sbase + p.o_ga[slot], p.gld, b0, nt * 8, lane);
             mma<T>(acc, af, bf[0], bf[1]);
           }
-          const int r = mt * 16 + gq, n = nt * 8 + 2 * tq;
+          const int n = nt * 8 + 2 * tq;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int rr = r + 8 * h;
-            if (rr >= p.dims[l]) continue;
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              if (n + j >= cols) continue;
-              const int idx = rr * WLD + n + j;
-              const float wn = St<T>::ld(at<T>(smem, p.o_w[l], idx)) + p.alpha * acc[2 * h + j];
-              const uint16_t hb = bits<T>(wn);
-              const uint32_t a = sbase + p.o_w[l] + 2 * idx;
-              for (int cc = 0; cc < C; ++cc) st_dsmem_u16(mapa(a, cc), hb);
+            const int rr = mt * 16 + gq + 8 * h;
+            if (rr >= p.dims[l] || n >= cols) continue;
+            const int idx = rr * WLD + n;
+            const uint32_t a = sbase + p.o_w[l] + 2 * idx;
+            if (n + 1 < cols) {
+              float w0, w1;
+              unpack2<T>(U32(p.o_w[l], idx), w0, w1);
+              const uint32_t v = bits2<T>(w0 + p.alpha * acc[2 * h], w1 + p.alpha * acc[2 * h + 1]);
+              for (int cc = 0; cc < C; ++cc) st_dsmem_u32(mapa(a, cc), v);
+            } else {
+              const uint16_t v = bits<T>(St<T>::ld(S(p.o_w[l])[idx]) + p.alpha * acc[2 * h]);
+              for (int cc = 0; cc < C; ++cc) st_dsmem_u16(mapa(a, cc), v);
             }
           }
         }
       }
+      trace(step, 9);
       if (more) {
         cp_async_wait_all();
         __syncthreads();
-        act_inplace<T, ACT>(smem, p.o_al, p.ald, kcnt, B);
+        activate_batch();
       }
       __syncthreads();
+      trace(step, 10);
     } else if (more) {
-      async_rows<T>(smem, p.o_al, p.ald, batch_x(step + 1) + (long long)k_lo * B, B, kcnt, 0, B);
-      async_rows<T>(smem, p.o_x[0], SLD, batch_y(step + 1), B, p.dims[0], c0, NCOL);
+      async_plain<T>(smem, p.o_al, p.ald, batch_x(step + 1) + (long long)k_lo * B, B, kcnt, B);
+      async_state<T, NCOL>(smem, p.o_x[0], batch_y(step + 1), B, p.dims[0], c0);
       cp_async_wait_all();
       __syncthreads();
-      act_inplace<T, ACT>(smem, p.o_al, p.ald, kcnt, B);
+      activate_batch();
       __syncthreads();
     }
+    trace(step, 11);
   }
 
   // ---- outputs: states / errors of the owned columns, weights, the trained batch ----
   if (p.update_weights) {
-    cluster_sync_all();  // every replica holds every CTA's broadcast tiles
+    cluster_sync_all();  // every replica holds every owner's new tiles
     if (cta == 0) {
       for (int l = 0; l < Lt; ++l) {
         const int cols = p.dims[l + 1];
+        T* dst = gw(l);
         for (int it = threadIdx.x; it < p.dims[l] * cols; it += NET_THREADS)
-          gw(l)[it] = at<T>(smem, p.o_w[l], (it / cols) * WLD + it % cols);
+          dst[it] = S(p.o_w[l])[(it / cols) * WLD + it % cols];
       }
     }
+    T* dst = gw(Lt);
     for (int it = threadIdx.x; it < dT * kcnt; it += NET_THREADS) {
       const int r = it / kcnt, k = it % kcnt;
-      gw(Lt)[(long long)r * dL + k_lo + k] = at<T>(smem, p.o_wt, r * p.wtld + k);
+      dst[(long long)r * dL + k_lo + k] = S(p.o_wt)[r * p.wtld + k];
     }
   }
-  constexpr int VPR = NCOL / 8;
   for (int l = 0; l <= Lt; ++l) {
     const bool write_x = (l >= 1) || (p.pool_y != nullptr);
     for (int it = threadIdx.x; it < p.dims[l] * VPR; it += NET_THREADS) {
       const int r = it / VPR, c = (it % VPR) * 8;
+      const int i = sw<NCOL>(r, c);
       if (write_x)
-        *reinterpret_cast<uint4*>(gx(l) + (long long)r * B + c0 + c) =
-            *reinterpret_cast<const uint4*>(smem + p.o_x[l] + 2 * (r * SLD + c));
-      *reinterpret_cast<uint4*>(ge(l) + (long long)r * B + c0 + c) =
-          *reinterpret_cast<const uint4*>(smem + p.o_e[l] + 2 * (r * SLD + c));
+        *reinterpret_cast<uint4*>(gx(l) + (long long)r * B + c0 + c) = *reinterpret_cast<const uint4*>(S(p.o_x[l]) + i);
+      *reinterpret_cast<uint4*>(ge(l) + (long long)r * B + c0 + c) = *reinterpret_cast<const uint4*>(S(p.o_e[l]) + i);
     }
   }
   if (p.pool_x != nullptr) {  // the trainer's x[L] holds the batch it trained on (trainer.py:509)
@@ -579,21 +640,16 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel(const __grid_consta
 }
 
 // ------------------------------------------------------------------- host
-struct Plan {
-  int C, NCOL, KS, KSP;
-  int smem;
-};
-
 template <typename T>
 int make_layout(NetParams<T>& p, int C, int NCOL) {
   const int L = p.L, Lt = L - 1;
   p.C = C;
   p.KS = ((p.dims[L] + C - 1) / C + 7) / 8 * 8;
   p.KSP = (p.KS + 15) / 16 * 16;
-  p.sld = NCOL + 8;
   p.wtld = p.KSP + 8;
   p.ald = ((p.B + 15) / 16) * 16 + 8;
   p.gld = p.ald;
+  p.nown = Lt > 0 ? (Lt + C - 1) / C : 0;
   int off = 0;
   auto take = [&](int bytes) {
     int o = off;
@@ -603,17 +659,19 @@ int make_layout(NetParams<T>& p, int C, int NCOL) {
   const int es = (int)sizeof(T);
   for (int l = 0; l < Lt; ++l) p.o_w[l] = take(p.rows16[l] * WLD * es);
   for (int l = 0; l <= Lt; ++l) {
-    p.o_x[l] = take(p.rows16[l] * p.sld * es);
-    p.o_a[l] = take(p.rows16[l] * p.sld * es);
-    p.o_e[l] = take(p.rows16[l] * p.sld * es);
+    p.o_x[l] = take(p.rows16[l] * NCOL * es);
+    p.o_a[l] = take(p.rows16[l] * NCOL * es);
+    p.o_e[l] = take(p.rows16[l] * NCOL * es);
   }
+  p.o_mu = take(p.rows16[Lt] * NCOL * es);
   p.o_wt = take(p.rows16[Lt] * p.wtld * es);
   p.o_al = take(p.KSP * p.ald * es);
   p.o_recv = take(C * p.rows16[Lt] * NCOL * 4);
-  p.o_ge = take(64 * p.gld * es);
-  p.o_ga = take(64 * p.gld * es);
-  // not aliased with the staging: its columns past B must stay zero for the K = 16 granule
-  p.o_mu = take(p.rows16[Lt] * p.sld * es);
+  p.o_gt = take(p.rows16[Lt] * p.gld * es);
+  for (int s = 0; s < p.nown; ++s) {
+    p.o_ge[s] = take(64 * p.gld * es);
+    p.o_ga[s] = take(64 * p.gld * es);
+  }
   p.smem_bytes = off;
   return off;
 }
@@ -640,7 +698,7 @@ int choose_plan(NetParams<T>& p, int want, int* ncol_out) {
 
 template <typename T, int ACT, int NCOL>
 int launch_net_t(NetParams<T>& p, cudaStream_t s) {
-  auto kern = net_kernel<T, ACT, NCOL>;
+  auto kern = net_kernel_act<T, ACT, NCOL>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem_bytes);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "net kernel smem attribute: %s", cudaGetErrorString(err));
   cudaLaunchConfig_t cfg = {};
@@ -691,6 +749,7 @@ int run_net(const ipc_net_t* net, const ipc_net_run_t* run, cudaStream_t s) {
   p.alpha = run->alpha;
   p.gamma = run->gamma;
   p.energy = run->energy;
+  p.phase_ns = run->phase_ns;
   int ncol = 0;
   int rc = choose_plan(p, run->cluster, &ncol);
   if (rc) return rc;
