@@ -225,3 +225,48 @@ def rel_inf(got: torch.Tensor, ref: torch.Tensor) -> float:
     if den == 0.0:
         return num
     return num / den
+
+
+# --------------------------------------------------------------------------
+# The whole training step with the reference GPU path's storage rounding.
+#
+# The reference trainer runs the fused operators on storage-dtype tensors
+# (trainer.py:601-674) after an eager storage-dtype forward sweep
+# (trainer.py:509-516).  Composing the single-operator restatements above in
+# that order gives the same rounding points, so a discontinuous f' (relu)
+# sees the same rounded states as the GPU kernels do.
+# --------------------------------------------------------------------------
+
+def train_step_storage(x_input, y_target, w, *, act: str, alpha: float, gamma: float, T: int, sdt: torch.dtype):
+    """One training step (forward sweep, T x (P, I), W with the last iteration's e) in storage dtype.
+
+    Inputs are CPU tensors; returns ``(x, w, e)`` as storage-dtype tensors."""
+    L = len(w)
+    w = [wi.to(sdt) for wi in w]
+    dims = [wi.shape[0] for wi in w] + [w[-1].shape[1]]
+    B = x_input.shape[1]
+    x = [torch.zeros((d, B), dtype=sdt) for d in dims]
+    x[L] = x_input.to(sdt)
+    for l in reversed(range(1, L)):
+        a = _rnd(act_forward(act, x[l + 1].double()), sdt)
+        x[l] = (w[l].double() @ a).to(sdt)
+    x[0] = y_target.to(sdt)
+    e = None
+    for t in range(T):
+        e = [pred_err_op(x[l + 1], w[l], x[l], act=act, sdt=sdt) for l in range(L)]
+        new_x = list(x)
+        for l in range(1, L):
+            new_x[l], _ = infer_update_op(x[l], e[l], w[l - 1], e[l - 1], act=act, gamma=gamma, sdt=sdt)
+        x = new_x
+        if t == T - 1:
+            w = [weight_update_op(w[l], e[l], x[l + 1], act=act, alpha=alpha, sdt=sdt) for l in range(L)]
+    return x, w, e
+
+
+def train_storage(batches, w, *, act: str, alpha: float, gamma: float, T: int, steps: int, sdt: torch.dtype,
+                  first_batch: int = 0):
+    x = e = None
+    for s in range(steps):
+        xi, yi = batches[(first_batch + s) % len(batches)]
+        x, w, e = train_step_storage(xi, yi, w, act=act, alpha=alpha, gamma=gamma, T=T, sdt=sdt)
+    return x, w, e
