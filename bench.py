@@ -356,7 +356,7 @@ def run_c2_e2e(args, model, dims, B, T, dtype, dev, rank, world):
     h2d(0, 0)
     for c in range(nchunks):
         slot = c % 2
-        if (c * chunk) % RESET_EVERY == 0:
+        if c % max(1, RESET_EVERY // chunk) == 0:
             for w, w0 in zip(model.w, w_init):
                 w.copy_(w0)
         if c + 1 < nchunks:
