@@ -131,6 +131,38 @@ int ipc_weight_apply(void* w, const float* dw, long long n, int dtype, void* str
 int ipc_forward(const void* x_up, const void* w, void* out, int M, int K, int B, int groups, int act, int dtype,
                 int algo, void* stream);
 
+/*
+ * General fused GEMM: one entry for every operator above, with the operand
+ * roles fixed by `mode` (all row-major, `groups` stacked contiguously):
+ *   IPC_MODE_PRED    a = W [M,K]     b = X_up/A_up [K,B]  aux = X_lo [M,B]  out = E [M,B]
+ *   IPC_MODE_FORWARD a = W [M,K]     b = X_up/A_up [K,B]  out [M,B]; aux2 = f(cast(out)) or NULL
+ *   IPC_MODE_INFER   a = W_low [K,M] b = E_low [K,B]      aux = E [M,B]  out = X [M,B] (in/out)
+ *                    aux2 = A_out or NULL, scale = gamma
+ *   IPC_MODE_WEIGHT  a = E [M,B]     b = X_up/A_up [K,B]  out = W [M,K] (in/out), scale = alpha
+ *   IPC_MODE_WDELTA  as WEIGHT with out = dw (fp32 [M,K])
+ * flags: IPC_FLAG_ACTIVATE_B applies f to b (otherwise b is a saved activation);
+ * IPC_FLAG_AOUT_STORED makes A_out = f(cast(x_new)), the value the recompute
+ * mode reads back (default f(x_new), tilelang_kernels.py:231);
+ * IPC_FLAG_ACCUMULATE adds into dw.  The tcgen05 kernel serves calls without
+ * IPC_FLAG_ACTIVATE_B.  No single reference counterpart: it subsumes the
+ * entries above.
+ */
+#define IPC_MODE_PRED 0
+#define IPC_MODE_INFER 1
+#define IPC_MODE_WEIGHT 2
+#define IPC_MODE_WDELTA 3
+#define IPC_MODE_FORWARD 4
+#define IPC_FLAG_ACTIVATE_B 1
+#define IPC_FLAG_AOUT_STORED 2
+#define IPC_FLAG_ACCUMULATE 4
+int ipc_fused_gemm(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K,
+                   int B, int groups, float scale, int flags, int act, int dtype, int algo, void* stream);
+
+/* First error a device-side bounded wait recorded since the last clear
+ * (IPC_OK if none; IPC_ERR_TIMEOUT when a pipeline wait gave up).  Synchronises
+ * with the device; clear != 0 resets the word.  No reference counterpart. */
+int ipc_device_status(int* status, int clear);
+
 /* A = cast(f(X)) over n elements (materialise a saved activation). */
 int ipc_activate(void* a, const void* x, long long n, int act, int dtype, void* stream);
 

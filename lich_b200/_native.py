@@ -28,6 +28,9 @@ DTYPE_NAMES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": t
                "half": torch.float16}
 ALGO_CODES = {"auto": 0, "simt": 1, "generic": 1, "tcgen05": 2, "outer": 3}
 
+MODE_PRED, MODE_INFER, MODE_WEIGHT, MODE_WDELTA, MODE_FORWARD = 0, 1, 2, 3, 4
+FLAG_ACTIVATE_B, FLAG_AOUT_STORED, FLAG_ACCUMULATE = 1, 2, 4
+
 NET_MAX_LAYERS = 8
 NET_TRACE_STEPS = 64
 NET_TRACE_PHASES = 12
@@ -35,7 +38,7 @@ NET_TRACE_PHASES = 12
 EXPORTED = (
     "ipc_abi_version", "ipc_last_error", "ipc_launch_count", "ipc_pred_err", "ipc_pred_err_saved",
     "ipc_forward", "ipc_infer_update", "ipc_weight_update", "ipc_weight_delta", "ipc_weight_apply",
-    "ipc_activate", "ipc_net_train", "ipc_net_plan",
+    "ipc_activate", "ipc_net_train", "ipc_net_plan", "ipc_fused_gemm", "ipc_device_status",
 )
 
 
@@ -107,6 +110,8 @@ def load() -> ctypes.CDLL:
         "ipc_activate": (i, [vp, vp, ll, i, i, vp]),
         "ipc_net_train": (i, [POINTER(IpcNet), POINTER(IpcNetRun), vp]),
         "ipc_net_plan": (i, [POINTER(IpcNet), i, POINTER(c_int), POINTER(c_int)]),
+        "ipc_fused_gemm": (i, [i, vp, vp, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp]),
+        "ipc_device_status": (i, [POINTER(c_int), i]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -171,6 +176,22 @@ def net_plan(dims, B: int, nets: int = 1, cluster: int = 0) -> tuple[int, int] |
     c, sm = c_int(0), c_int(0)
     rc = load().ipc_net_plan(ctypes.byref(desc), int(cluster), ctypes.byref(c), ctypes.byref(sm))
     return (c.value, sm.value) if rc == IPC_OK else None
+
+
+def fused_gemm(mode: int, a, b, out, aux=None, aux2=None, *, M: int, K: int, B: int, groups: int = 1,
+               scale: float = 0.0, flags: int = 0, act: str = "identity", dtype=torch.float16, algo: str = "auto",
+               device=None) -> None:
+    """``ipc_fused_gemm`` on the current stream (operand roles per mode: include/ipc_b200.h)."""
+    check(load().ipc_fused_gemm(int(mode), ptr(a), ptr(b), ptr(out), ptr(aux), ptr(aux2), int(M), int(K), int(B),
+                                int(groups), float(scale), int(flags), act_code(act), dtype_code(dtype),
+                                ALGO_CODES[algo], stream_handle(device)))
+
+
+def device_status(clear: bool = True) -> int:
+    """First device-side error code recorded by a bounded wait (0 if none); synchronises."""
+    v = c_int(0)
+    check(load().ipc_device_status(ctypes.byref(v), int(clear)))
+    return v.value
 
 
 def launch_count() -> int:

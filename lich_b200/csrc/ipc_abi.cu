@@ -91,7 +91,7 @@ static int pred_err_impl(const void* x_up, const void* w, const void* x_lo, void
   p.out = e; p.gsOut = (long long)M * B;
   p.aux = x_lo; p.gsAux = (long long)M * B;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (tc_eligible(MODE_P, M, K, B, dtype, algo)) return launch_tc(p, MODE_P, bact, act, dtype, s);
+  if (tc_eligible(MODE_P, M, K, B, dtype, algo, bact)) return launch_tc(p, MODE_P, act, dtype, s);
   if (algo == IPC_ALGO_TCGEN05) return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: shape/dtype not eligible (M=%d K=%d B=%d dtype=%d)", M, K, B, dtype);
   return launch_generic(p, MODE_P, bact, act, dtype, s);
 }
@@ -119,7 +119,7 @@ int ipc_forward(const void* x_up, const void* w, void* out, int M, int K, int B,
   p.Mg = M; p.Ng = B; p.Kg = K; p.groups = groups;
   p.out = out; p.gsOut = (long long)M * B;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (tc_eligible(MODE_F, M, K, B, dtype, algo)) return launch_tc(p, MODE_F, true, act, dtype, s);
+  if (tc_eligible(MODE_F, M, K, B, dtype, algo, true)) return launch_tc(p, MODE_F, act, dtype, s);
   if (algo == IPC_ALGO_TCGEN05) return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: shape/dtype not eligible (M=%d K=%d B=%d dtype=%d)", M, K, B, dtype);
   return launch_generic(p, MODE_F, true, act, dtype, s);
 }
@@ -140,7 +140,7 @@ int ipc_infer_update(void* x, const void* e, const void* w_low, const void* e_lo
   p.aux2 = a_out; p.gsAux2 = (long long)M * B;
   p.scale = gamma;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (tc_eligible(MODE_I, M, K, B, dtype, algo)) return launch_tc(p, MODE_I, false, act, dtype, s);
+  if (tc_eligible(MODE_I, M, K, B, dtype, algo, false)) return launch_tc(p, MODE_I, act, dtype, s);
   if (algo == IPC_ALGO_TCGEN05) return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: shape/dtype not eligible (M=%d K=%d B=%d dtype=%d)", M, K, B, dtype);
   return launch_generic(p, MODE_I, false, act, dtype, s);
 }
@@ -163,7 +163,7 @@ static int weight_impl(void* out, const void* e, const void* x_up, int M, int K,
   p.scale = alpha;
   p.accumulate = accumulate;
   const int mode = delta ? MODE_WD : MODE_W;
-  if (tc_eligible(mode, M, K, B, dtype, algo)) return launch_tc(p, mode, bact, act, dtype, s);
+  if (tc_eligible(mode, M, K, B, dtype, algo, bact)) return launch_tc(p, mode, act, dtype, s);
   if (algo == IPC_ALGO_TCGEN05) return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: shape/dtype not eligible (M=%d K=%d B=%d dtype=%d)", M, K, B, dtype);
   return launch_generic(p, mode, bact, act, dtype, s);
 }
@@ -194,6 +194,55 @@ int ipc_activate(void* a, const void* x, long long n, int act, int dtype, void* 
   if (n == 0) return IPC_OK;
   IPC_REQUIRE(a && x, "null operand pointer");
   return launch_activate(a, x, n, act, dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ipc_fused_gemm(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K, int B,
+                   int groups, float scale, int flags, int act, int dtype, int algo, void* stream) {
+  int rc = common_checks(M, K, B, groups, act, dtype, algo);
+  if (rc) return rc;
+  IPC_REQUIRE(mode >= MODE_P && mode <= MODE_F, "unknown mode %d", mode);
+  IPC_REQUIRE(algo != IPC_ALGO_OUTER || mode == MODE_W || mode == MODE_WD,
+              "IPC_ALGO_OUTER applies to the weight update only");
+  const bool bact = (flags & IPC_FLAG_ACTIVATE_B) != 0;
+  IPC_REQUIRE(!(mode == MODE_I && bact), "the inference update takes E_low as is");
+  GemmArgs p{};
+  p.scale = scale;
+  p.accumulate = (flags & IPC_FLAG_ACCUMULATE) != 0;
+  p.a_out_from_stored = (flags & IPC_FLAG_AOUT_STORED) != 0;
+  p.groups = groups;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (mode == MODE_W || mode == MODE_WD) {
+    if (M == 0 || K == 0) return IPC_OK;
+    IPC_REQUIRE(out && (B == 0 || (a && b)), "null operand pointer");
+    if (algo == IPC_ALGO_OUTER || (algo == IPC_ALGO_AUTO && B <= 16))
+      return launch_outer(out, a, b, M, K, B, groups, scale, bact, mode == MODE_WD, p.accumulate, act, dtype, s);
+    p.A = a; p.lda = B; p.gsA = (long long)M * B;
+    p.Bm = b; p.ldb = B; p.gsB = (long long)K * B;
+    p.Mg = M; p.Ng = K; p.Kg = B;
+    p.out = out; p.gsOut = (long long)M * K;
+  } else {
+    if (M == 0 || B == 0) return IPC_OK;
+    IPC_REQUIRE(out && (K == 0 || (a && b)), "null operand pointer");
+    IPC_REQUIRE(mode != MODE_P || aux, "prediction error needs X_lo (aux)");
+    IPC_REQUIRE(mode != MODE_I || aux, "inference update needs E (aux)");
+    p.A = a; p.lda = (mode == MODE_I) ? M : K; p.gsA = (long long)M * K;
+    p.Bm = b; p.ldb = B; p.gsB = (long long)K * B;
+    p.Mg = M; p.Ng = B; p.Kg = K;
+    p.out = out; p.gsOut = (long long)M * B;
+    p.aux = aux; p.gsAux = (long long)M * B;
+    p.aux2 = aux2; p.gsAux2 = (long long)M * B;
+  }
+  if (tc_eligible(mode, M, K, B, dtype, algo, bact)) return launch_tc(p, mode, act, dtype, s);
+  if (algo == IPC_ALGO_TCGEN05)
+    return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: not eligible (mode=%d M=%d K=%d B=%d dtype=%d activate_b=%d)",
+                     mode, M, K, B, dtype, (int)bact);
+  return launch_generic(p, mode, bact, act, dtype, s);
+}
+
+int ipc_device_status(int* status, int clear) {
+  int rc = require_sm100();
+  if (rc) return rc;
+  return read_device_status(status, clear);
 }
 
 }  // extern "C"

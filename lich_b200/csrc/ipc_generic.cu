@@ -9,7 +9,7 @@
 //   I  (tilelang_kernels.py:180-265)  A = W_low^T       B = E_low[K,B]        X += g(-E + f'(X) C) [, A_out]
 //   W  (tilelang_kernels.py:268-349)  A = E[M,B]        B = f(X_up)^T          W = cast(W + a C)
 //   WD (no reference counterpart)     as W, but dw (+)= a C in fp32
-//   F  (trainer.py:512-515, 828-833)  as P                                   OUT = cast(C)
+//   F  (trainer.py:512-515, 828-833)  as P                                   OUT = cast(C) [, A_out = f(OUT)]
 // Padding of the activated operand stays zero (tilelang_kernels.py:165-167).
 #include <cstdio>
 
@@ -36,13 +36,15 @@ __device__ __forceinline__ void epilogue(const GemmArgs& p, int g, int m, int n,
     const float ev = St<T>::ld(e[idx]);
     const float xn = xv + p.scale * (-ev + act_df<ACT>(xv) * acc);
     x[idx] = St<T>::st(xn);
-    if (p.aux2 != nullptr) reinterpret_cast<T*>(p.aux2)[g * p.gsAux2 + idx] = St<T>::st(act_f<ACT>(xn));
+    if (p.aux2 != nullptr)
+      reinterpret_cast<T*>(p.aux2)[g * p.gsAux2 + idx] = St<T>::st(act_f<ACT>(p.a_out_from_stored ? rnd<T>(xn) : xn));
   } else if constexpr (MODE == MODE_W) {
     T* w = reinterpret_cast<T*>(p.out) + g * p.gsOut;
     w[idx] = St<T>::st(St<T>::ld(w[idx]) + p.scale * acc);
   } else if constexpr (MODE == MODE_F) {
     T* o = reinterpret_cast<T*>(p.out) + g * p.gsOut;
     o[idx] = St<T>::st(acc);
+    if (p.aux2 != nullptr) reinterpret_cast<T*>(p.aux2)[g * p.gsAux2 + idx] = St<T>::st(act_f<ACT>(rnd<T>(acc)));
   } else {
     float* dw = reinterpret_cast<float*>(p.out) + g * p.gsOut;
     const float v = p.scale * acc;
@@ -237,7 +239,7 @@ int launch_one(const GemmArgs& p, cudaStream_t s) {
 int launch_generic(const GemmArgs& p, int mode, bool bact, int act, int dtype, cudaStream_t s) {
   if (p.Mg <= 0 || p.Ng <= 0 || p.groups <= 0) return IPC_OK;  // empty output: nothing to do
   IPC_DISPATCH_DT(dtype, TT, {
-    if (!bact && mode != MODE_I) {
+    if (!bact && mode != MODE_I && !(mode == MODE_F && p.aux2 != nullptr)) {
       // the activation only enters through the B operand -> one instantiation
       switch (mode) {
         case MODE_P: return launch_one<TT, IPC_ACT_IDENTITY, MODE_P, false>(p, s);
@@ -253,7 +255,8 @@ int launch_generic(const GemmArgs& p, int mode, bool bact, int act, int dtype, c
         case MODE_I: return launch_one<TT, AC, MODE_I, false>(p, s);
         case MODE_W: return launch_one<TT, AC, MODE_W, true>(p, s);
         case MODE_WD: return launch_one<TT, AC, MODE_WD, true>(p, s);
-        case MODE_F: return launch_one<TT, AC, MODE_F, true>(p, s);
+        case MODE_F:
+          return bact ? launch_one<TT, AC, MODE_F, true>(p, s) : launch_one<TT, AC, MODE_F, false>(p, s);
         default: return set_error(IPC_ERR_ARG, "bad GEMM mode %d", mode);
       }
     });

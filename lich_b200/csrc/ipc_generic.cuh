@@ -25,6 +25,7 @@ struct GemmArgs {
   long long gsAux2;
   float scale;      // I: gamma   W/WD: alpha
   int accumulate;   // WD
+  int a_out_from_stored;  // I: A_out = f(cast(x_new)) (what recompute mode reads back) instead of f(x_new)
 };
 
 int launch_generic(const GemmArgs& p, int mode, bool bact, int act, int dtype, cudaStream_t s);

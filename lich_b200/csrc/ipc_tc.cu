@@ -1,9 +1,528 @@
+// tcgen05 / TMEM / TMA tensor-core kernel for the fused P / I / W / forward
+// GEMMs of wide layers (16-bit storage, fp32 accumulation).
+//
+// One persistent CTA per SM walks the output tiles (128 x BN, BN = 256 or
+// 128).  Warp roles:
+//   warp 0      TMA producer: a 4-stage ring of 64-deep K blocks, 128-byte
+//               swizzled tiles loaded with cp.async.bulk.tensor (no multicast).
+//   warp 1      TMEM owner and MMA issuer: one thread issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M = 128, N = BN, K = 16)
+//               into one of two TMEM accumulators (2 x BN fp32 columns);
+//               tcgen05.commit releases smem stages / publishes accumulators.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator rows (thread = row),
+//               the mode's fused element-wise epilogue, global stores; the
+//               second accumulator lets the next tile's MMAs run meanwhile.
+// All 32 lanes of warps 0 and 1 walk their loops (so the final CTA barrier is
+// reached convergently); lane 0 alone issues TMA, MMA and commits.
+// Operand orientation per mode (UMMA "K-major" = reduction dim contiguous):
+//   P, F : A = W [M, K]          K-major    B = A_up [K, N]        MN-major
+//   I    : A = W_low [K, M]      MN-major   B = E_low [K, N]       MN-major
+//   W, WD: A = E [M, Bt]         K-major    B = A_up [Kw, Bt]      K-major
+// The B operand is taken as stored (a saved activation): applying f inside
+// the GEMM would repeat it M/128 times per element; callers materialise
+// f(X) once (ipc_activate, or the A_out of the state update / forward sweep).
+// Tails in M, N, K are handled by TMA zero fill and epilogue masks; inner
+// dimensions must be multiples of 8 elements (16-byte TMA strides).
+//
+// Every mbarrier wait is bounded (about 2 s of %globaltimer); on expiry the
+// kernel records IPC_ERR_TIMEOUT in a device status word, every role stops
+// issuing work, and TMEM is freed before the CTA returns (ipc_device_status
+// reads the word).
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <mutex>
+
 #include "ipc_common.cuh"
+#include "ipc_generic.cuh"
 #include "ipc_tc.cuh"
 
 namespace ipc {
-bool tc_eligible(int, int, int, int, int, int) { return false; }
-int launch_tc(const GemmArgs&, int, bool, int, int, cudaStream_t) {
-  return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path not built");
+
+__device__ int g_device_status = 0;  // first error code raised by a device-side bounded wait
+
+namespace {
+
+constexpr int TC_BM = 128;
+constexpr int TC_BK = 64;
+constexpr int TC_STAGES = 4;
+constexpr int TC_THREADS = 192;
+constexpr long long TC_WAIT_NS = 2000000000LL;
+
+struct TcParams {
+  int Mg, Ng, Kg, groups;
+  int tiles_m, tiles_n, tiles;
+  void* out;
+  long long ld_out, gs_out;
+  const void* aux;
+  long long gs_aux;
+  void* aux2;
+  long long gs_aux2;
+  float scale;
+  int accumulate;
+  int a_out_from_stored;  // I: A_out = f(cast(x_new)) (what recompute mode reads back) instead of f(x_new)
+};
+
+// ------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t saddr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ long long now_ns() {
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and the device status set) if the phase never completes.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = now_ns();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (now_ns() - t0 > TC_WAIT_NS) {
+      atomicCAS(&g_device_status, 0, IPC_ERR_TIMEOUT);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+template <typename T>
+struct Vec8 {
+  static __device__ __forceinline__ void ld(const T* p, float (&v)[8]) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const T* h = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = St<T>::ld(h[j]);
+  }
+  static __device__ __forceinline__ void st(T* p, const float (&v)[8]) {
+    uint4 raw;
+    T* h = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = St<T>::st(v[j]);
+    *reinterpret_cast<uint4*>(p) = raw;
+  }
+};
+
+// Fused epilogue for 8 consecutive columns [n, n+8) of output row m.
+template <typename T, int ACT, int MODE>
+__device__ __forceinline__ void epi8(const TcParams& p, int g, int m, int n, const float (&acc)[8]) {
+  const long long idx = (long long)m * p.ld_out + n;
+  if constexpr (MODE == MODE_P) {
+    float xl[8], ev[8];
+    Vec8<T>::ld(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + idx, xl);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ev[j] = xl[j] - rnd<T>(acc[j]);
+    Vec8<T>::st(reinterpret_cast<T*>(p.out) + g * p.gs_out + idx, ev);
+  } else if constexpr (MODE == MODE_I) {
+    float xv[8], ev[8], xn[8];
+    T* xp = reinterpret_cast<T*>(p.out) + g * p.gs_out + idx;
+    Vec8<T>::ld(xp, xv);
+    Vec8<T>::ld(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + idx, ev);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xn[j] = xv[j] + p.scale * (-ev[j] + act_df<ACT>(xv[j]) * acc[j]);
+    Vec8<T>::st(xp, xn);
+    if (p.aux2 != nullptr) {
+      float an[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) an[j] = act_f<ACT>(p.a_out_from_stored ? rnd<T>(xn[j]) : xn[j]);
+      Vec8<T>::st(reinterpret_cast<T*>(p.aux2) + g * p.gs_aux2 + idx, an);
+    }
+  } else if constexpr (MODE == MODE_W) {
+    float wv[8];
+    T* wp = reinterpret_cast<T*>(p.out) + g * p.gs_out + idx;
+    Vec8<T>::ld(wp, wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wv[j] += p.scale * acc[j];
+    Vec8<T>::st(wp, wv);
+  } else if constexpr (MODE == MODE_WD) {
+    float4* dw = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + g * p.gs_out + idx);
+    float4 a = make_float4(p.scale * acc[0], p.scale * acc[1], p.scale * acc[2], p.scale * acc[3]);
+    float4 b = make_float4(p.scale * acc[4], p.scale * acc[5], p.scale * acc[6], p.scale * acc[7]);
+    if (p.accumulate) {
+      const float4 a0 = dw[0], b0 = dw[1];
+      a.x += a0.x; a.y += a0.y; a.z += a0.z; a.w += a0.w;
+      b.x += b0.x; b.y += b0.y; b.z += b0.z; b.w += b0.w;
+    }
+    dw[0] = a;
+    dw[1] = b;
+  } else {  // MODE_F
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = acc[j];
+    Vec8<T>::st(reinterpret_cast<T*>(p.out) + g * p.gs_out + idx, o);
+    if (p.aux2 != nullptr) {
+      float an[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) an[j] = act_f<ACT>(rnd<T>(acc[j]));
+      Vec8<T>::st(reinterpret_cast<T*>(p.aux2) + g * p.gs_aux2 + idx, an);
+    }
+  }
+}
+
+template <typename T, int ACT, int MODE, int BN>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ TcParams p) {
+  constexpr bool A_MN = (MODE == MODE_I);
+  constexpr bool B_MN = (MODE == MODE_P || MODE == MODE_I || MODE == MODE_F);
+  constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
+  constexpr uint32_t B_BYTES = BN * TC_BK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
+  // instruction descriptor: fp32 accumulate, A/B fp16 or bf16, majors, N, M = 128
+  constexpr uint32_t FMT = std::is_same<T, __half>::value ? 0u : 1u;
+  constexpr uint32_t IDESC = (1u << 4) | (FMT << 7) | (FMT << 10) | ((A_MN ? 1u : 0u) << 15) |
+                             ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TC_STAGES * STAGE_BYTES);
+  // bars: full[S], empty[S], tfull[2], tempty[2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * TC_STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t full0 = saddr(bars), empty0 = saddr(bars + TC_STAGES);
+  const uint32_t tfull0 = saddr(bars + 2 * TC_STAGES), tempty0 = saddr(bars + 2 * TC_STAGES + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tempty0 + 8 * b, 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int nk = (p.Kg + TC_BK - 1) / TC_BK;
+  const int tiles_mn = p.tiles_m * p.tiles_n;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    }
+    int s = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+      const int g = t / tiles_mn, r = t % tiles_mn;
+      const int m0 = (r % p.tiles_m) * TC_BM, n0 = (r / p.tiles_m) * BN;
+      for (int kb = 0; kb < nk; ++kb) {
+        ok = mbar_wait(empty0 + 8 * s, phase ^ 1, abort_flag);
+        __syncwarp();
+        if (!ok) break;
+        if (lane == 0) {
+          const uint32_t full = full0 + 8 * s;
+          mbar_expect_tx(full, STAGE_BYTES);
+          const uint32_t sa = saddr(smem + s * STAGE_BYTES), sb = sa + A_BYTES;
+          const int k0 = kb * TC_BK;
+          if constexpr (A_MN) {
+            tma_load_3d(sa, &tmA, full, m0, k0, g);
+            tma_load_3d(sa + A_BYTES / 2, &tmA, full, m0 + 64, k0, g);
+          } else {
+            tma_load_3d(sa, &tmA, full, k0, m0, g);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sb + j * (64 * TC_BK * 2), &tmB, full, n0 + 64 * j, k0, g);
+          } else {
+            tma_load_3d(sb, &tmB, full, k0, n0, g);
+          }
+        }
+        __syncwarp();
+        if (++s == TC_STAGES) { s = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer -------------------------------
+    int s = 0, acc = 0;
+    uint32_t phase = 0, aphase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+      ok = mbar_wait(tempty0 + 8 * acc, aphase ^ 1, abort_flag);
+      __syncwarp();
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < nk; ++kb) {
+        ok = mbar_wait(full0 + 8 * s, phase, abort_flag);
+        __syncwarp();
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sa = saddr(smem + s * STAGE_BYTES), sb = sa + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < TC_BK / 16; ++kk) {
+            // K-major: +32 B per 16-element step inside the 128-byte swizzle row.
+            // MN-major: +2 groups of 8 K-rows (2 KB) per step; 64-element MN blocks 8 KB apart.
+            const uint64_t ad = A_MN ? smem_desc(sa + kk * 2048, 64 * TC_BK * 2, 1024) : smem_desc(sa + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc(sb + kk * 2048, 64 * TC_BK * 2, 1024) : smem_desc(sb + kk * 32, 16, 1024);
+            tc_mma(d_tmem, ad, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(empty0 + 8 * s);  // stage free once these MMAs have read it
+        }
+        __syncwarp();
+        if (++s == TC_STAGES) { s = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      if (lane == 0) tc_commit(tfull0 + 8 * acc);  // accumulator ready
+      __syncwarp();
+      if (++acc == 2) { acc = 0; aphase ^= 1; }
+    }
+  } else {
+    // ------------------------------- epilogue --------------------------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t aphase = 0;
+    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
+      const bool ok = mbar_wait(tfull0 + 8 * acc, aphase, abort_flag);
+      __syncwarp();
+      if (!ok) break;
+      tc_fence_after();
+      const int g = t / tiles_mn, r = t % tiles_mn;
+      const int m = (r % p.tiles_m) * TC_BM + 32 * q + lane;
+      const int n0 = (r / p.tiles_m) * BN;
+      const uint32_t trow = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t raw[32];
+        tmem_ld32(trow + 32 * c, raw);
+        if (m < p.Mg) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const int n = n0 + 32 * c + 8 * v;
+            if (n < p.Ng) {
+              float a8[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[8 * v + j]);
+              epi8<T, ACT, MODE>(p, g, m, n, a8);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty0 + 8 * acc);
+      if (++acc == 2) { acc = 0; aphase ^= 1; }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+  }
+}
+
+// ------------------------------------------------------------------- host
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 3-D map over a [groups][rows][inner] row-major array (element strides ld, gs).
+int make_map(CUtensorMap* map, const void* base, int dtype, long long inner, long long rows, long long groups,
+             long long ld, long long gs, int box_inner, int box_rows) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return set_error(IPC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)groups};
+  const cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(gs * 2)};
+  const cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt = dtype == IPC_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(IPC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return IPC_OK;
+}
+
+int num_sms() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (n[dev] == 0) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev] > 0 ? n[dev] : 148;
+}
+
+template <typename T, int ACT, int MODE, int BN>
+int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s) {
+  constexpr bool A_MN = (MODE == MODE_I);
+  constexpr bool B_MN = (MODE == MODE_P || MODE == MODE_I || MODE == MODE_F);
+  CUtensorMap ta, tb;
+  int rc;
+  // A operand: rows are the M side (K-major) or the K side (MN-major)
+  if (A_MN)
+    rc = make_map(&ta, a.A, dtype, a.Mg, a.Kg, a.groups, a.lda, a.gsA, 64, TC_BK);
+  else
+    rc = make_map(&ta, a.A, dtype, a.Kg, a.Mg, a.groups, a.lda, a.gsA, TC_BK, TC_BM);
+  if (rc) return rc;
+  if (B_MN)
+    rc = make_map(&tb, a.Bm, dtype, a.Ng, a.Kg, a.groups, a.ldb, a.gsB, 64, TC_BK);
+  else
+    rc = make_map(&tb, a.Bm, dtype, a.Kg, a.Ng, a.groups, a.ldb, a.gsB, TC_BK, BN);
+  if (rc) return rc;
+  TcParams p{};
+  p.Mg = a.Mg; p.Ng = a.Ng; p.Kg = a.Kg; p.groups = a.groups;
+  p.tiles_m = (a.Mg + TC_BM - 1) / TC_BM;
+  p.tiles_n = (a.Ng + BN - 1) / BN;
+  p.tiles = p.tiles_m * p.tiles_n * a.groups;
+  p.out = a.out; p.ld_out = a.Ng; p.gs_out = a.gsOut;
+  p.aux = a.aux; p.gs_aux = a.gsAux;
+  p.aux2 = a.aux2; p.gs_aux2 = a.gsAux2;
+  p.scale = a.scale; p.accumulate = a.accumulate;
+  p.a_out_from_stored = a.a_out_from_stored;
+  constexpr int STAGE_BYTES = (TC_BM + BN) * TC_BK * 2;
+  const int smem = TC_STAGES * STAGE_BYTES + 1024 + 256;
+  auto kern = tc_gemm_kernel<T, ACT, MODE, BN>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "tcgen05 kernel smem attribute: %s", cudaGetErrorString(err));
+  const int grid = p.tiles < num_sms() ? p.tiles : num_sms();
+  kern<<<grid, TC_THREADS, smem, s>>>(ta, tb, p);
+  count_launch();
+  return check_launch("tcgen05 GEMM");
+}
+
+template <typename T, int MODE, int BN>
+int dispatch_act(const GemmArgs& a, int act, int dtype, cudaStream_t s) {
+  if constexpr (MODE == MODE_P || MODE == MODE_W || MODE == MODE_WD) {
+    return launch_tc_t<T, IPC_ACT_IDENTITY, MODE, BN>(a, dtype, s);  // activation only in I / F epilogues
+  } else {
+    IPC_DISPATCH_ACT(act, AC, { return launch_tc_t<T, AC, MODE, BN>(a, dtype, s); });
+  }
+  return IPC_OK;
+}
+
+template <typename T, int BN>
+int dispatch_mode(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s) {
+  switch (mode) {
+    case MODE_P: return dispatch_act<T, MODE_P, BN>(a, act, dtype, s);
+    case MODE_I: return dispatch_act<T, MODE_I, BN>(a, act, dtype, s);
+    case MODE_W: return dispatch_act<T, MODE_W, BN>(a, act, dtype, s);
+    case MODE_WD: return dispatch_act<T, MODE_WD, BN>(a, act, dtype, s);
+    case MODE_F: return dispatch_act<T, MODE_F, BN>(a, act, dtype, s);
+    default: return set_error(IPC_ERR_ARG, "bad GEMM mode %d", mode);
+  }
+}
+
+}  // namespace
+
+bool tc_eligible(int mode, int M, int K, int B, int dtype, int algo, bool b_activated) {
+  if (algo != IPC_ALGO_AUTO && algo != IPC_ALGO_TCGEN05) return false;
+  if (dtype != IPC_DT_F16 && dtype != IPC_DT_BF16) return false;
+  if (b_activated) return false;  // f on the B operand is materialised once by the caller
+  int Mg = M, Ng = B, Kg = K;
+  if (mode == MODE_W || mode == MODE_WD) { Ng = K; Kg = B; }
+  if (Mg < 1 || Ng < 1 || Kg < 1) return false;
+  if (M % 8 || K % 8 || B % 8) return false;  // 16-byte row strides for TMA and the epilogue vectors
+  if (algo == IPC_ALGO_AUTO) {
+    // below ~128 x 256 x 256 the generic kernel's lower latency wins
+    if (Mg < 128 || Ng < 128 || Kg < 64) return false;
+    if ((double)Mg * Ng * Kg < 128.0 * 256 * 256) return false;
+  }
+  return true;
+}
+
+int launch_tc(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s) {
+  if (a.Mg <= 0 || a.Ng <= 0 || a.groups <= 0) return IPC_OK;
+  if (a.Kg <= 0) return launch_generic(a, mode, false, act, dtype, s);  // nothing to multiply
+  const bool wide = a.Ng >= 256;
+  if (dtype == IPC_DT_F16)
+    return wide ? dispatch_mode<__half, 256>(a, mode, act, dtype, s) : dispatch_mode<__half, 128>(a, mode, act, dtype, s);
+  return wide ? dispatch_mode<__nv_bfloat16, 256>(a, mode, act, dtype, s)
+              : dispatch_mode<__nv_bfloat16, 128>(a, mode, act, dtype, s);
+}
+
+int read_device_status(int* status, int clear) {
+  int v = 0;
+  cudaError_t err = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int));
+  if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "device status read: %s", cudaGetErrorString(err));
+  if (clear && v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+  }
+  if (status) *status = v;
+  return IPC_OK;
+}
+
 }  // namespace ipc
