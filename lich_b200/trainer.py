@@ -131,6 +131,10 @@ class TileLangIPC:
         self._x_grouped: list[torch.Tensor] = []
         self._e_grouped: list[torch.Tensor] = []
         self._a_grouped: list[torch.Tensor] | None = None
+        # activation cache of the 16-bit operator path: ac[l] = cast(f(x[l])), written by the forward
+        # sweep and the state-update epilogues, read as the stored operand of P / W (tensor-core GEMMs)
+        self._ac: list[torch.Tensor] | None = None
+        self._ac_grouped: list[torch.Tensor] = []
         self._runtime_plan_key: tuple | None = None
         self._pred_singleton_kernels: list[object | None] = []
         self._inf_singleton_kernels: list[object | None] = []
@@ -209,6 +213,9 @@ class TileLangIPC:
         self._x_grouped, self._e_grouped = [], []
         self.a = None if self.recompute_activation else [None] * len(dims)
         self._a_grouped = None if self.recompute_activation else []
+        use_ac = self._acache_path(B)
+        self._ac = [None] * len(dims) if use_ac else None  # type: ignore[list-item]
+        self._ac_grouped = []
         grouped_states = set()
         for gi, gr in enumerate(self._layer_groups):
             xbuf = torch.zeros((gr.state_count, gr.width, B), device=dev, dtype=dt)
@@ -217,12 +224,16 @@ class TileLangIPC:
             self._e_grouped.append(ebuf)
             if self._a_grouped is not None:
                 self._a_grouped.append(torch.zeros_like(xbuf))
+            if use_ac:
+                self._ac_grouped.append(torch.zeros_like(xbuf))
             for z, layer in enumerate(gr.state_indices):
                 grouped_states.add(layer)
                 self.x[layer] = xbuf[z]
                 self.e[layer] = ebuf[z]
                 if self.a is not None:
                     self.a[layer] = self._a_grouped[gi][z]
+                if use_ac:
+                    self._ac[layer] = self._ac_grouped[gi][z]
         for layer, d in enumerate(dims):
             if layer in grouped_states:
                 continue
@@ -230,7 +241,20 @@ class TileLangIPC:
             self.e[layer] = torch.zeros_like(self.x[layer])
             if self.a is not None:
                 self.a[layer] = torch.zeros_like(self.x[layer])
+            if use_ac:
+                self._ac[layer] = torch.zeros_like(self.x[layer])
         self._runtime_plan_key = None
+
+    def _acache_path(self, B: int) -> bool:
+        """16-bit recompute mode off the persistent kernel: P / W read a cached f(cast(x)) so their GEMMs
+        take stored operands (the tensor-core kernel); numerically the recompute semantics."""
+        return (self.cfg.dtype in (torch.float16, torch.bfloat16) and self.recompute_activation
+                and not self.net_kernel_eligible(B))
+
+    def _fg(self, mode, a, b, out, aux=None, aux2=None, *, M, K, B, groups=1, scale=0.0, flags=0):
+        N.fused_gemm(mode, a, b, out, aux, aux2, M=M, K=K, B=B, groups=groups, scale=scale, flags=flags,
+                     act=self.cfg.activation, dtype=self.cfg.dtype, algo=getattr(self.cfg.kernel, "backend", "auto"),
+                     device=self.device)
 
     def _prepare_runtime_plan(self, batch: int) -> None:
         """Build the kernel-call plan once per (dims, batch, activation, dtype, mode)."""
@@ -350,8 +374,16 @@ class TileLangIPC:
         self.x[-1].copy_(x_input)
         if self.a is not None:
             self.a[-1].copy_(self.act.forward(self.x[-1]))
-        for l in reversed(range(1, self.L)):
-            self._fwd_singleton_kernels[l](self.x[l + 1], self.w[l], self.x[l])
+        d = self.cfg.dims
+        if self._ac is not None:
+            N.check(N.load().ipc_activate(N.ptr(self._ac[-1]), N.ptr(self.x[-1]), self.x[-1].numel(), self.act.code,
+                                          N.dtype_code(self.cfg.dtype), N.stream_handle(self.device)))
+            for l in reversed(range(1, self.L)):
+                self._fg(N.MODE_FORWARD, self.w[l], self._ac[l + 1], self.x[l], None, self._ac[l],
+                         M=d[l], K=d[l + 1], B=B)
+        else:
+            for l in reversed(range(1, self.L)):
+                self._fwd_singleton_kernels[l](self.x[l + 1], self.w[l], self.x[l])
         self.x[0].copy_(y_target)
 
     @torch.no_grad()
@@ -377,6 +409,15 @@ class TileLangIPC:
         return {}
 
     def _phase_p(self):
+        if self._ac is not None:
+            B, d = int(self.x[0].shape[1]), self.cfg.dims
+            for gi, gr in enumerate(self._layer_groups):
+                xs, es = self._x_grouped[gi], self._e_grouped[gi]
+                self._fg(N.MODE_PRED, self._w_grouped[gi], self._ac_grouped[gi][1:], es[:-1], xs[:-1],
+                         M=gr.width, K=gr.width, B=B, groups=gr.count)
+            for l, _ in self._pred_singleton_ops:
+                self._fg(N.MODE_PRED, self.w[l], self._ac[l + 1], self.e[l], self.x[l], M=d[l], K=d[l + 1], B=B)
+            return
         for gi, gr in enumerate(self._layer_groups):
             xs, es = self._x_grouped[gi], self._e_grouped[gi]
             self._pred_group_kernels[gi](xs[1:], self._w_grouped[gi], xs[:-1], es[:-1])
@@ -384,6 +425,17 @@ class TileLangIPC:
             k(self.x[l + 1], self.w[l], self.x[l], self.e[l])
 
     def _phase_i(self):
+        if self._ac is not None:
+            B, d = int(self.x[0].shape[1]), self.cfg.dims
+            g = self.cfg.gamma
+            for gi, gr in enumerate(self._layer_groups):
+                xs, es, ws = self._x_grouped[gi], self._e_grouped[gi], self._w_grouped[gi]
+                self._fg(N.MODE_INFER, ws, es[:-1], xs[1:], es[1:], self._ac_grouped[gi][1:], M=gr.width, K=gr.width,
+                         B=B, groups=gr.count, scale=g, flags=N.FLAG_AOUT_STORED)
+            for l, _ in self._inf_singleton_ops:
+                self._fg(N.MODE_INFER, self.w[l - 1], self.e[l - 1], self.x[l], self.e[l], self._ac[l], M=d[l],
+                         K=d[l - 1], B=B, scale=g, flags=N.FLAG_AOUT_STORED)
+            return
         for gi, gr in enumerate(self._layer_groups):
             xs, es, ws = self._x_grouped[gi], self._e_grouped[gi], self._w_grouped[gi]
             if self.a is None:
@@ -397,6 +449,16 @@ class TileLangIPC:
                 k(self.x[l], self.e[l], self.w[l - 1], self.e[l - 1], self.a[l])
 
     def _phase_w(self):
+        if self._ac is not None:
+            B, d = int(self.x[0].shape[1]), self.cfg.dims
+            al = self.cfg.alpha
+            for gi, gr in enumerate(self._layer_groups):
+                self._fg(N.MODE_WEIGHT, self._e_grouped[gi][:-1], self._ac_grouped[gi][1:], self._w_grouped[gi],
+                         M=gr.width, K=gr.width, B=B, groups=gr.count, scale=al)
+            for l in range(self.L):
+                if l not in self._edge_to_group:
+                    self._fg(N.MODE_WEIGHT, self.e[l], self._ac[l + 1], self.w[l], M=d[l], K=d[l + 1], B=B, scale=al)
+            return
         for gi, gr in enumerate(self._layer_groups):
             es, ws = self._e_grouped[gi], self._w_grouped[gi]
             src = self._x_grouped[gi][1:] if self.a is None else self._a_grouped[gi][1:]
@@ -539,12 +601,12 @@ class TileLangIPC:
         if self.x is None or self.e is None:
             raise RuntimeError("Call initialize_batch before precompile")
         self._prepare_runtime_plan(int(self.x[-1].shape[1]))
-        saved = [t.clone() for t in self.w + self.x + self.e] + \
-                ([v.clone() for v in self.a if v is not None] if self.a is not None else [])
+        live = list(self.w + self.x + self.e) + ([v for v in self.a if v is not None] if self.a is not None else []) \
+            + (list(self._ac) if self._ac is not None else [])
+        saved = [t.clone() for t in live]
         done = self.steps_done
         self.step_initialized(collect_metrics=False)
         torch.cuda.synchronize(self.device)
-        live = list(self.w + self.x + self.e) + ([v for v in self.a if v is not None] if self.a is not None else [])
         for dst, src in zip(live, saved):
             dst.copy_(src)
         self.steps_done = done

@@ -291,3 +291,25 @@ def test_metrics_and_errors():
         m.initialize_batch(xb[:100].to(DEV, torch.float16), yb.to(DEV, torch.float16))
     r = m.step(xb.to(DEV, torch.float16), yb.to(DEV, torch.float16))
     assert r["max_abs_error"] > 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_wide_operator_path_tensor_cores(dtype):
+    """A miniature of the wide configuration (hidden 512, B = 512): the operator path with the
+    activation cache, whose GEMMs run on the tcgen05 kernel; one training step vs the fp32 oracle."""
+    from lich_b200 import synthetic as S
+    dims = (104, 512, 512, 512, 1024)
+    w0 = S.fan_in_normal(dims, seed=31)
+    pool = S.batch_pool(1024, 104, 512, count=1, seed=32)
+    m = _model(dims, "tanh", dtype, alpha=1e-3)
+    assert not m.net_kernel_eligible(512)
+    _set_w(m, w0)
+    m.train_step(pool[0][0].to(DEV, dtype), pool[0][1].to(DEV, dtype), T=4)
+    from lich_b200 import _native as N
+    assert N.device_status() == 0
+    wq, bq = _oracle_inputs(w0, pool, dtype)
+    x, w, e, _ = O.train(bq, wq, act="tanh", alpha=1e-3, gamma=0.5, T=4, steps=1)
+    for l in range(len(w)):
+        assert O.rel_inf(m.w[l].cpu(), w[l]) <= 1e-2, ("w", l)
+    for l in range(len(x)):
+        assert O.rel_inf(m.x[l].cpu(), x[l]) <= 1e-2, ("x", l)
