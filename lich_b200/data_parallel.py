@@ -1,0 +1,108 @@
+"""Batch-sharded data-parallel iPC training (one process per GPU, torch.distributed / NCCL).
+
+Prediction errors and state updates are column-local, so each rank runs the
+forward sweep and the T inference iterations on its own slice of the batch
+with no communication.  The only coupling is the weight update, a sum over
+all batch columns:
+
+    W[l] += alpha * sum_ranks E_r[l] f(x_r[l+1])^T
+
+Each rank forms its fp32 partial ``dW_r[l]`` (``ipc_weight_delta`` /
+``IPC_MODE_WDELTA``, tensor cores for wide layers), the partials are summed
+with one all-reduce per layer (issued as soon as that layer's partial is
+ready, so the reductions of earlier layers overlap the GEMMs of later ones),
+and every rank applies the same sum (``ipc_weight_apply``), keeping the
+replicas identical.  The reference is single-GPU; this is the scaling path of
+the wide configuration (batch 65536 over 1/2/4/8 B200s).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _native as N
+from .trainer import IPCConfig, TileLangIPC
+
+
+def allreduce_deltas(deltas: list[torch.Tensor], group=None, *, async_op: bool = True):
+    """Sum-all-reduce each tensor of ``deltas`` in place (one collective per tensor, in list order).
+
+    Returns the work handles (empty if ``async_op`` is False or there is one rank)."""
+    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return []
+    handles = []
+    for d in deltas:
+        h = dist.all_reduce(d, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
+        if async_op:
+            handles.append(h)
+    return handles
+
+
+class DataParallelIPC:
+    """Replicated weights, batch shards, one fp32 dW all-reduce per layer per training step."""
+
+    def __init__(self, cfg: IPCConfig, *, device: torch.device, group=None, seed: int = 0,
+                 model: TileLangIPC | None = None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        self.model = model if model is not None else TileLangIPC(cfg, device=device, seed=seed)
+        self.cfg = self.model.cfg
+        if self.world > 1:
+            for w in self.model.w:  # identical replicas to start from
+                dist.broadcast(w, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        self._dw = self._alloc_deltas()
+
+    def _alloc_deltas(self) -> list[torch.Tensor]:
+        d = self.cfg.dims
+        flat = torch.zeros(sum(d[l] * d[l + 1] for l in range(len(d) - 1)), dtype=torch.float32,
+                           device=self.model.w[0].device)
+        out, off = [], 0
+        for l in range(len(d) - 1):
+            n = d[l] * d[l + 1]
+            out.append(flat[off:off + n].view(d[l], d[l + 1]))
+            off += n
+        return out
+
+    # -- the two kernel calls of the update (overridable for host-side tests) --
+    def _delta(self, l: int, dw: torch.Tensor) -> None:
+        """dw = alpha * E[l] f(x[l+1])^T over this rank's columns, fp32."""
+        m = self.model
+        d = self.cfg.dims
+        B = int(m.x[0].shape[1])
+        if m._ac is not None:  # cached activation: a stored operand (tensor-core kernel when wide)
+            N.fused_gemm(N.MODE_WDELTA, m.e[l], m._ac[l + 1], dw, M=d[l], K=d[l + 1], B=B, scale=self.cfg.alpha,
+                         act=self.cfg.activation, dtype=self.cfg.dtype, device=m.device)
+        else:
+            N.fused_gemm(N.MODE_WDELTA, m.e[l], m.x[l + 1], dw, M=d[l], K=d[l + 1], B=B, scale=self.cfg.alpha,
+                         flags=N.FLAG_ACTIVATE_B, act=self.cfg.activation, dtype=self.cfg.dtype, device=m.device)
+
+    def _apply(self, l: int, dw: torch.Tensor) -> None:
+        w = self.model.w[l]
+        N.check(N.load().ipc_weight_apply(w.data_ptr(), dw.data_ptr(), w.numel(), N.dtype_code(w.dtype),
+                                          N.stream_handle(w.device)))
+
+    @torch.no_grad()
+    def train_step(self, x_local: torch.Tensor, y_local: torch.Tensor, *, T: int = 4) -> None:
+        """Forward sweep + T inference iterations on the local shard, then the all-reduced weight update
+        with the last iteration's errors and states (the oracle schedule, full batch = all shards)."""
+        if T < 1:
+            raise ValueError("T must be >= 1")
+        m = self.model
+        m.initialize_batch(x_local, y_local)
+        for _ in range(T):
+            m.step_initialized(update_weights=False)
+        L = len(self.cfg.dims) - 1
+        order = sorted(range(L), key=lambda l: -self._dw[l].numel())  # biggest reductions start first
+        handles = []
+        for l in order:
+            self._delta(l, self._dw[l])
+            handles += allreduce_deltas([self._dw[l]], self.group, async_op=True)
+        for h in handles:
+            h.wait()
+        for l in order:
+            self._apply(l, self._dw[l])
+        m.steps_done += 1
+
+    def state_dict(self) -> dict:
+        return self.model.state_dict()

@@ -9,3 +9,8 @@ if str(ROOT) not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100) and the built native library")
+    # The native library is a build output (not committed): build it once if this checkout has none.
+    from lich_b200.build import LIB, build
+
+    if not LIB.exists():
+        build()
