@@ -484,6 +484,89 @@ def run_c5(args, world, rank, local):
     return line
 
 
+C3_SIZES = (64, 256, 1024, 4096, 8192)
+C3_BATCHES = (128, 1024, 8192, 65536)
+
+
+def run_c3(args, world, rank, local):
+    """each fused operator isolated, M = K in C3_SIZES, B in C3_BATCHES, fp16, tanh.
+
+    Kernels: P (prediction error), I (state update), W-saved (A = f(X) given) and W-recompute
+    (f(X) materialised once, then the saved-A GEMM: both launches timed).  L2 is flushed (256 MB
+    write) before every timed launch; each point is the median of the repetitions."""
+    from lich_b200 import _native as N
+
+    dev = torch.device("cuda", local)
+    dt = torch.float16
+    pk = peaks()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    sizes = [int(s) for s in args.sizes.split(",")] if args.sizes else C3_SIZES
+    batches = [int(b) for b in args.batches.split(",")] if args.batches else C3_BATCHES
+    points = []
+    launches0 = N.launch_count()
+    for M in sizes:
+        for B in batches:
+            K = M
+            g = torch.Generator(device=dev).manual_seed(M * 7 + B)
+            x_up = torch.randn((K, B), generator=g, device=dev).to(dt)
+            w = (torch.randn((M, K), generator=g, device=dev) / K ** 0.5).to(dt)
+            x_lo = torch.randn((M, B), generator=g, device=dev).to(dt)
+            e = torch.empty_like(x_lo)
+            a_up = torch.empty_like(x_up)
+            N.check(N.load().ipc_activate(a_up.data_ptr(), x_up.data_ptr(), x_up.numel(), 1, 1, N.stream_handle(dev)))
+            w_low = (torch.randn((K, M), generator=g, device=dev) / M ** 0.5).to(dt)
+            e_low = torch.randn((K, B), generator=g, device=dev).to(dt)
+            x = x_lo.clone()
+            ws = w.clone()
+            kinds = {
+                "P": (lambda: N.fused_gemm(N.MODE_PRED, w, a_up, e, x_lo, M=M, K=K, B=B, dtype=dt, device=dev),
+                      (M * K + K * B + 2 * M * B) * 2),
+                "I": (lambda: N.fused_gemm(N.MODE_INFER, w_low, e_low, x, e, M=M, K=K, B=B, scale=0.5, act="tanh",
+                                           dtype=dt, device=dev), (3 * M * B + K * M + K * B) * 2),
+                "W_saved": (lambda: N.fused_gemm(N.MODE_WEIGHT, e, a_up, ws, M=M, K=K, B=B, scale=1e-4, dtype=dt,
+                                                 device=dev), (2 * M * K + M * B + K * B) * 2),
+                "W_recompute": (lambda: (N.check(N.load().ipc_activate(a_up.data_ptr(), x_up.data_ptr(),
+                                                                      x_up.numel(), 1, 1, N.stream_handle(dev))),
+                                         N.fused_gemm(N.MODE_WEIGHT, e, a_up, ws, M=M, K=K, B=B, scale=1e-4,
+                                                      dtype=dt, device=dev)),
+                                (2 * M * K + M * B + 3 * K * B) * 2),
+            }
+            reps = 3 if 2.0 * M * K * B > 1e12 else 7
+            for name, (fn, nbytes) in kinds.items():
+                fn()
+                times = []
+                for _ in range(reps):
+                    flush.fill_(1.0)
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    fn()
+                    b.record()
+                    b.synchronize()
+                    times.append(a.elapsed_time(b))
+                ms = statistics.median(times)
+                flop = 2.0 * M * K * B
+                t_tc, t_hbm = flop / (pk["bf16_tflops"] * 1e12), nbytes / (pk["hbm_gbs"] * 1e9)
+                bound = "tensor" if t_tc >= t_hbm else "hbm"
+                points.append({"kernel": name, "M": M, "K": K, "B": B, "ms": round(ms, 5),
+                               "tflops": round(flop / ms / 1e9, 2), "gbs": round(nbytes / ms / 1e6, 1),
+                               "bound": bound, "frac": round(max(t_tc, t_hbm) / (ms * 1e-3), 4),
+                               "algo": "tcgen05" if (M >= 128 and K >= 64 and B >= 128 and
+                                                     2.0 * M * K * B >= 2 * 128 * 256 * 256) else "mma.sync"})
+            del x_up, w, x_lo, e, a_up, w_low, e_low, x, ws
+            torch.cuda.empty_cache()
+    big = [p for p in points if p["bound"] == "tensor" and p["M"] >= 4096]
+    head = max(big, key=lambda p: p["frac"]) if big else max(points, key=lambda p: p["frac"])
+    return {"metric": "per-kernel microbench (configs[2]): fraction of roofline", "value": head["frac"],
+            "unit": "fraction of measured peak", "n_gpus": 1, "steps": len(points), "warmup": 1,
+            "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "configs[2]: P / I / W isolated, M=K in {64..8192}, B in {128..65536}, fp16, tanh",
+                       "l2": "256 MB buffer written before every timed launch"},
+            "roofline": {"bound": head["bound"], "peak_tflops": pk["bf16_tflops"], "peak_gbs": pk["hbm_gbs"],
+                         "peak_source": pk["source"], "headline_point": head},
+            "points": points, "gpu_launches": int(N.launch_count() - launches0)}
+
+
 def run_reference(args, world, rank):
     """--impl reference: the reference algorithm on the host CPU (rank 0 only)."""
     if rank != 0:
@@ -520,8 +603,11 @@ def main():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c5"], default="c2",
-                    help="c2: configs[1] hidden-64 (default); c5: configs[4] wide data-parallel")
+    ap.add_argument("--config", choices=["c2", "c3", "c5"], default="c2",
+                    help="c2: configs[1] hidden-64 (default); c3: configs[2] per-kernel microbench; "
+                         "c5: configs[4] wide data-parallel")
+    ap.add_argument("--sizes", default="", help="c3: comma-separated M=K list")
+    ap.add_argument("--batches", default="", help="c3: comma-separated B list")
     ap.add_argument("--batch", type=int, default=0, help="c5: global batch (default 65536)")
     ap.add_argument("--depth", type=int, default=6)
     ap.add_argument("--act", default="tanh")
@@ -539,7 +625,8 @@ def main():
     if args.config == "c5" and "--steps" not in sys.argv:
         args.steps = 5
     world, rank, local = dist_setup(args)
-    line = run_c5(args, world, rank, local) if args.config == "c5" else run_c2(args, world, rank, local)
+    runners = {"c2": run_c2, "c3": run_c3, "c5": run_c5}
+    line = runners[args.config](args, world, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
