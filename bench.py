@@ -488,6 +488,19 @@ C3_SIZES = (64, 256, 1024, 4096, 8192)
 C3_BATCHES = (128, 1024, 8192, 65536)
 
 
+def _c3_algo(kind, M, K, B):
+    """Which kernel IPC_ALGO_AUTO picks for a c3 point (the library's tcgen05 eligibility rule)."""
+    weight = kind.startswith("W")
+    mg, ng, kg = (M, K, B) if weight else (M, B, K)
+    if weight and kg >= 1024 and mg >= 16 and ng >= 16:
+        return "tcgen05 split-K" if -(-mg // 128) * -(-ng // 128) < 74 else "tcgen05"
+    if weight and B <= 16:
+        return "outer"
+    if mg >= 128 and ng >= 128 and kg >= 64 and mg * ng * kg >= 128 * 256 * 256:
+        return "tcgen05"
+    return "mma.sync"
+
+
 def run_c3(args, world, rank, local):
     """each fused operator isolated, M = K in C3_SIZES, B in C3_BATCHES, fp16, tanh.
 
@@ -518,17 +531,18 @@ def run_c3(args, world, rank, local):
             e_low = torch.randn((K, B), generator=g, device=dev).to(dt)
             x = x_lo.clone()
             ws = w.clone()
+            scratch = torch.empty(N.SPLITK_WORKSPACE_BYTES // 4, dtype=torch.float32, device=dev)
             kinds = {
                 "P": (lambda: N.fused_gemm(N.MODE_PRED, w, a_up, e, x_lo, M=M, K=K, B=B, dtype=dt, device=dev),
                       (M * K + K * B + 2 * M * B) * 2),
                 "I": (lambda: N.fused_gemm(N.MODE_INFER, w_low, e_low, x, e, M=M, K=K, B=B, scale=0.5, act="tanh",
                                            dtype=dt, device=dev), (3 * M * B + K * M + K * B) * 2),
                 "W_saved": (lambda: N.fused_gemm(N.MODE_WEIGHT, e, a_up, ws, M=M, K=K, B=B, scale=1e-4, dtype=dt,
-                                                 device=dev), (2 * M * K + M * B + K * B) * 2),
+                                                 device=dev, workspace=scratch), (2 * M * K + M * B + K * B) * 2),
                 "W_recompute": (lambda: (N.check(N.load().ipc_activate(a_up.data_ptr(), x_up.data_ptr(),
                                                                       x_up.numel(), 1, 1, N.stream_handle(dev))),
                                          N.fused_gemm(N.MODE_WEIGHT, e, a_up, ws, M=M, K=K, B=B, scale=1e-4,
-                                                      dtype=dt, device=dev)),
+                                                      dtype=dt, device=dev, workspace=scratch)),
                                 (2 * M * K + M * B + 3 * K * B) * 2),
             }
             reps = 3 if 2.0 * M * K * B > 1e12 else 7
@@ -550,9 +564,8 @@ def run_c3(args, world, rank, local):
                 points.append({"kernel": name, "M": M, "K": K, "B": B, "ms": round(ms, 5),
                                "tflops": round(flop / ms / 1e9, 2), "gbs": round(nbytes / ms / 1e6, 1),
                                "bound": bound, "frac": round(max(t_tc, t_hbm) / (ms * 1e-3), 4),
-                               "algo": "tcgen05" if (M >= 128 and K >= 64 and B >= 128 and
-                                                     2.0 * M * K * B >= 2 * 128 * 256 * 256) else "mma.sync"})
-            del x_up, w, x_lo, e, a_up, w_low, e_low, x, ws
+                               "algo": _c3_algo(name, M, K, B)})
+            del x_up, w, x_lo, e, a_up, w_low, e_low, x, ws, scratch
             torch.cuda.empty_cache()
     big = [p for p in points if p["bound"] == "tensor" and p["M"] >= 4096]
     head = max(big, key=lambda p: p["frac"]) if big else max(points, key=lambda p: p["frac"])

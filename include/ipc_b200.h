@@ -158,6 +158,23 @@ int ipc_forward(const void* x_up, const void* w, void* out, int M, int K, int B,
 int ipc_fused_gemm(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K,
                    int B, int groups, float scale, int flags, int act, int dtype, int algo, void* stream);
 
+/*
+ * ipc_fused_gemm with a caller-owned fp32 workspace (16-byte aligned device
+ * memory, contents need not be initialised).  A weight update (WEIGHT /
+ * WDELTA) whose output has fewer 128-row tiles than half the SMs and whose
+ * batch reduction is long is split over the batch ("split-K"): each split
+ * writes an fp32 partial tile into the workspace and a second pass sums the
+ * partials in split order (deterministic) and applies the epilogue.  The
+ * number of splits is bounded by workspace_bytes / (groups*M*K*4), so any
+ * size works; 0 bytes is exactly ipc_fused_gemm.  Other modes ignore the
+ * workspace.  Calls sharing a workspace must be ordered on one stream.  No
+ * reference counterpart: the reference's weight kernel reduces the batch
+ * inside one CTA per output tile (tilelang_kernels.py:269-320).
+ */
+int ipc_fused_gemm_ws(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K,
+                      int B, int groups, float scale, int flags, int act, int dtype, int algo, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
 /* First error a device-side bounded wait recorded since the last clear
  * (IPC_OK if none; IPC_ERR_TIMEOUT when a pipeline wait gave up).  Synchronises
  * with the device; clear != 0 resets the word.  No reference counterpart. */

@@ -7,7 +7,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, Structure, c_char_p, c_float, c_int, c_longlong, c_ulonglong, c_void_p
+from ctypes import POINTER, Structure, c_char_p, c_float, c_int, c_longlong, c_size_t, c_ulonglong, c_void_p
 from pathlib import Path
 
 import torch
@@ -31,6 +31,11 @@ ALGO_CODES = {"auto": 0, "simt": 1, "generic": 1, "tcgen05": 2, "outer": 3}
 MODE_PRED, MODE_INFER, MODE_WEIGHT, MODE_WDELTA, MODE_FORWARD = 0, 1, 2, 3, 4
 FLAG_ACTIVATE_B, FLAG_AOUT_STORED, FLAG_ACCUMULATE = 1, 2, 4
 
+# Split-K scratch that covers every shape the weight update splits: a split happens only with fewer
+# than half the SMs' worth of 128 x 128 output tiles, and splits x tiles stays below 148 + tiles, so the
+# fp32 partials never exceed 222 tiles x 64 KiB.
+SPLITK_WORKSPACE_BYTES = 16 << 20
+
 NET_MAX_LAYERS = 8
 NET_TRACE_STEPS = 64
 NET_TRACE_PHASES = 12
@@ -39,6 +44,7 @@ EXPORTED = (
     "ipc_abi_version", "ipc_last_error", "ipc_launch_count", "ipc_pred_err", "ipc_pred_err_saved",
     "ipc_forward", "ipc_infer_update", "ipc_weight_update", "ipc_weight_delta", "ipc_weight_apply",
     "ipc_activate", "ipc_net_train", "ipc_net_plan", "ipc_fused_gemm", "ipc_device_status",
+    "ipc_fused_gemm_ws",
 )
 
 
@@ -112,6 +118,7 @@ def load() -> ctypes.CDLL:
         "ipc_net_plan": (i, [POINTER(IpcNet), i, POINTER(c_int), POINTER(c_int)]),
         "ipc_fused_gemm": (i, [i, vp, vp, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp]),
         "ipc_device_status": (i, [POINTER(c_int), i]),
+        "ipc_fused_gemm_ws": (i, [i, vp, vp, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp, c_size_t, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -180,11 +187,18 @@ def net_plan(dims, B: int, nets: int = 1, cluster: int = 0) -> tuple[int, int] |
 
 def fused_gemm(mode: int, a, b, out, aux=None, aux2=None, *, M: int, K: int, B: int, groups: int = 1,
                scale: float = 0.0, flags: int = 0, act: str = "identity", dtype=torch.float16, algo: str = "auto",
-               device=None) -> None:
+               device=None, workspace=None) -> None:
     """``ipc_fused_gemm`` on the current stream (operand roles per mode: include/ipc_b200.h)."""
-    check(load().ipc_fused_gemm(int(mode), ptr(a), ptr(b), ptr(out), ptr(aux), ptr(aux2), int(M), int(K), int(B),
-                                int(groups), float(scale), int(flags), act_code(act), dtype_code(dtype),
-                                ALGO_CODES[algo], stream_handle(device)))
+    if workspace is None:
+        check(load().ipc_fused_gemm(int(mode), ptr(a), ptr(b), ptr(out), ptr(aux), ptr(aux2), int(M), int(K), int(B),
+                                    int(groups), float(scale), int(flags), act_code(act), dtype_code(dtype),
+                                    ALGO_CODES[algo], stream_handle(device)))
+    else:  # fp32 scratch for split-K partial tiles (``ipc_fused_gemm_ws``)
+        nbytes = workspace.numel() * workspace.element_size()
+        check(load().ipc_fused_gemm_ws(int(mode), ptr(a), ptr(b), ptr(out), ptr(aux), ptr(aux2), int(M), int(K),
+                                       int(B), int(groups), float(scale), int(flags), act_code(act),
+                                       dtype_code(dtype), ALGO_CODES[algo], ptr(workspace), nbytes,
+                                       stream_handle(device)))
 
 
 def device_status(clear: bool = True) -> int:

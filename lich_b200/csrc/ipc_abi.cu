@@ -196,8 +196,9 @@ int ipc_activate(void* a, const void* x, long long n, int act, int dtype, void* 
   return launch_activate(a, x, n, act, dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int ipc_fused_gemm(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K, int B,
-                   int groups, float scale, int flags, int act, int dtype, int algo, void* stream) {
+static int fused_gemm_impl(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K,
+                           int B, int groups, float scale, int flags, int act, int dtype, int algo, float* ws,
+                           size_t ws_bytes, void* stream) {
   int rc = common_checks(M, K, B, groups, act, dtype, algo);
   if (rc) return rc;
   IPC_REQUIRE(mode >= MODE_P && mode <= MODE_F, "unknown mode %d", mode);
@@ -232,11 +233,27 @@ int ipc_fused_gemm(int mode, const void* a, const void* b, void* out, const void
     p.aux = aux; p.gsAux = (long long)M * B;
     p.aux2 = aux2; p.gsAux2 = (long long)M * B;
   }
-  if (tc_eligible(mode, M, K, B, dtype, algo, bact)) return launch_tc(p, mode, act, dtype, s);
+  const bool splitk = ws != nullptr && (mode == MODE_W || mode == MODE_WD);
+  if (tc_eligible(mode, M, K, B, dtype, algo, bact, splitk)) return launch_tc(p, mode, act, dtype, s, ws, ws_bytes);
   if (algo == IPC_ALGO_TCGEN05)
     return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: not eligible (mode=%d M=%d K=%d B=%d dtype=%d activate_b=%d)",
                      mode, M, K, B, dtype, (int)bact);
   return launch_generic(p, mode, bact, act, dtype, s);
+}
+
+int ipc_fused_gemm(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K, int B,
+                   int groups, float scale, int flags, int act, int dtype, int algo, void* stream) {
+  return fused_gemm_impl(mode, a, b, out, aux, aux2, M, K, B, groups, scale, flags, act, dtype, algo, nullptr, 0,
+                         stream);
+}
+
+int ipc_fused_gemm_ws(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K,
+                      int B, int groups, float scale, int flags, int act, int dtype, int algo, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  IPC_REQUIRE(workspace != nullptr || workspace_bytes == 0, "workspace_bytes > 0 with a null workspace");
+  IPC_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 16 == 0, "workspace must be 16-byte aligned");
+  return fused_gemm_impl(mode, a, b, out, aux, aux2, M, K, B, groups, scale, flags, act, dtype, algo,
+                         static_cast<float*>(workspace), workspace_bytes, stream);
 }
 
 int ipc_device_status(int* status, int clear) {

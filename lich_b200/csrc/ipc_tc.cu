@@ -49,6 +49,8 @@ constexpr int TC_STAGES = 4;
 constexpr int TC_THREADS = 192;
 constexpr long long TC_WAIT_NS = 2000000000LL;
 
+constexpr int TC_RASTER = 16;  // M-tiles per raster group: a wave covers ~16 x 9 tiles, both operands stay in L2
+
 struct TcParams {
   int Mg, Ng, Kg, groups;
   int tiles_m, tiles_n, tiles;
@@ -61,6 +63,10 @@ struct TcParams {
   float scale;
   int accumulate;
   int a_out_from_stored;  // I: A_out = f(cast(x_new)) (what recompute mode reads back) instead of f(x_new)
+  // split-K (weight update with few output tiles): `splits` K ranges of `kps` 64-deep blocks each; the
+  // fp32 partial tiles go to ws[split][group][m][n] and ws_reduce_kernel applies the epilogue
+  int splits, kps;
+  float* ws;
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -132,6 +138,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Tile t -> (group, first row, first column).  Rows are walked in bands of
+// TC_RASTER M-tiles, all N-tiles of a band before the next band, so the CTAs of
+// one wave share a few A row-blocks and B column-blocks in L2.
+// With split-K the split index is the fastest-varying part of t.
+__device__ __forceinline__ void tile_coords(const TcParams& p, int t, int bn, int& g, int& m0, int& n0, int& s) {
+  s = t % p.splits;
+  t /= p.splits;
+  const int tiles_mn = p.tiles_m * p.tiles_n;
+  g = t / tiles_mn;
+  const int r = t % tiles_mn;
+  const int band = r / (TC_RASTER * p.tiles_n);
+  const int first_m = band * TC_RASTER;
+  const int band_m = min(TC_RASTER, p.tiles_m - first_m);
+  const int within = r - band * TC_RASTER * p.tiles_n;
+  m0 = (first_m + within % band_m) * TC_BM;
+  n0 = (within / band_m) * bn;
 }
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
@@ -266,7 +290,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int nk = (p.Kg + TC_BK - 1) / TC_BK;
-  const int tiles_mn = p.tiles_m * p.tiles_n;
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -278,9 +301,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint32_t phase = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
-      const int g = t / tiles_mn, r = t % tiles_mn;
-      const int m0 = (r % p.tiles_m) * TC_BM, n0 = (r / p.tiles_m) * BN;
-      for (int kb = 0; kb < nk; ++kb) {
+      int g, m0, n0, sp;
+      tile_coords(p, t, BN, g, m0, n0, sp);
+      const int kb_end = min(nk, (sp + 1) * p.kps);
+      for (int kb = sp * p.kps; kb < kb_end; ++kb) {
         ok = mbar_wait(empty0 + 8 * s, phase ^ 1, abort_flag);
         __syncwarp();
         if (!ok) break;
@@ -317,7 +341,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
-      for (int kb = 0; kb < nk; ++kb) {
+      const int sp = t % p.splits;
+      const int kb_begin = sp * p.kps, kb_end = min(nk, (sp + 1) * p.kps);
+      for (int kb = kb_begin; kb < kb_end; ++kb) {
         ok = mbar_wait(full0 + 8 * s, phase, abort_flag);
         __syncwarp();
         if (!ok) break;
@@ -330,7 +356,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             // MN-major: +2 groups of 8 K-rows (2 KB) per step; 64-element MN blocks 8 KB apart.
             const uint64_t ad = A_MN ? smem_desc(sa + kk * 2048, 64 * TC_BK * 2, 1024) : smem_desc(sa + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? smem_desc(sb + kk * 2048, 64 * TC_BK * 2, 1024) : smem_desc(sb + kk * 32, 16, 1024);
-            tc_mma(d_tmem, ad, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+            tc_mma(d_tmem, ad, bd, IDESC, (kb > kb_begin || kk > 0) ? 1u : 0u);
           }
           tc_commit(empty0 + 8 * s);  // stage free once these MMAs have read it
         }
@@ -352,9 +378,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       __syncwarp();
       if (!ok) break;
       tc_fence_after();
-      const int g = t / tiles_mn, r = t % tiles_mn;
-      const int m = (r % p.tiles_m) * TC_BM + 32 * q + lane;
-      const int n0 = (r / p.tiles_m) * BN;
+      int g, m0, n0, sp;
+      tile_coords(p, t, BN, g, m0, n0, sp);
+      const int m = m0 + 32 * q + lane;
       const uint32_t trow = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -365,10 +391,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int v = 0; v < 4; ++v) {
             const int n = n0 + 32 * c + 8 * v;
             if (n < p.Ng) {
-              float a8[8];
+              if (p.splits > 1) {  // fp32 partial of this K range; the reduce pass applies the epilogue
+                float4* dst = reinterpret_cast<float4*>(
+                    p.ws + (((long long)sp * p.groups + g) * p.Mg + m) * (long long)p.Ng + n);
+                dst[0] = make_float4(__uint_as_float(raw[8 * v]), __uint_as_float(raw[8 * v + 1]),
+                                     __uint_as_float(raw[8 * v + 2]), __uint_as_float(raw[8 * v + 3]));
+                dst[1] = make_float4(__uint_as_float(raw[8 * v + 4]), __uint_as_float(raw[8 * v + 5]),
+                                     __uint_as_float(raw[8 * v + 6]), __uint_as_float(raw[8 * v + 7]));
+              } else {
+                float a8[8];
 #pragma unroll
-              for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[8 * v + j]);
-              epi8<T, ACT, MODE>(p, g, m, n, a8);
+                for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[8 * v + j]);
+                epi8<T, ACT, MODE>(p, g, m, n, a8);
+              }
             }
           }
         }
@@ -425,8 +460,38 @@ int num_sms() {
   return n[dev] > 0 ? n[dev] : 148;
 }
 
+// Split-K second pass: out = epilogue(sum over splits of the fp32 partials), summed in split order
+// (deterministic).  W: W = cast(W + scale * sum); WD: dw = (accumulate ? dw : 0) + scale * sum.
+template <typename T, int MODE>
+__global__ void ws_reduce_kernel(const float* __restrict__ ws, int splits, long long n4, void* out, float scale,
+                                 int accumulate) {
+  const float4* part = reinterpret_cast<const float4*>(ws);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    float4 acc = part[i];
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 v = part[(long long)sp * n4 + i];
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    if constexpr (MODE == MODE_WD) {
+      float4* dw = reinterpret_cast<float4*>(out) + i;
+      float4 o = make_float4(scale * acc.x, scale * acc.y, scale * acc.z, scale * acc.w);
+      if (accumulate) {
+        const float4 d = *dw;
+        o.x += d.x; o.y += d.y; o.z += d.z; o.w += d.w;
+      }
+      *dw = o;
+    } else {
+      T* w = reinterpret_cast<T*>(out) + 4 * i;
+      w[0] = St<T>::st(St<T>::ld(w[0]) + scale * acc.x);
+      w[1] = St<T>::st(St<T>::ld(w[1]) + scale * acc.y);
+      w[2] = St<T>::st(St<T>::ld(w[2]) + scale * acc.z);
+      w[3] = St<T>::st(St<T>::ld(w[3]) + scale * acc.w);
+    }
+  }
+}
+
 template <typename T, int ACT, int MODE, int BN>
-int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s) {
+int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t ws_bytes) {
   constexpr bool A_MN = (MODE == MODE_I);
   constexpr bool B_MN = (MODE == MODE_P || MODE == MODE_I || MODE == MODE_F);
   CUtensorMap ta, tb;
@@ -452,6 +517,25 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s) {
   p.aux2 = a.aux2; p.gs_aux2 = a.gsAux2;
   p.scale = a.scale; p.accumulate = a.accumulate;
   p.a_out_from_stored = a.a_out_from_stored;
+  // split-K: a weight update with fewer output tiles than half the SMs and a long batch reduction
+  const int nk = (a.Kg + TC_BK - 1) / TC_BK;
+  p.splits = 1;
+  p.kps = nk;
+  p.ws = nullptr;
+  if ((MODE == MODE_W || MODE == MODE_WD) && ws != nullptr && p.tiles < num_sms() / 2 && nk >= 8 &&
+      a.gsOut == (long long)a.Mg * a.Ng) {  // the reduce pass walks out as one dense [groups][M][N] array
+    const long long tile_bytes = (long long)a.groups * a.Mg * a.Ng * 4;
+    int splits = (num_sms() + p.tiles - 1) / p.tiles;
+    splits = min(splits, nk / 4);
+    const long long fit = (long long)(ws_bytes / (size_t)tile_bytes);
+    if (fit < splits) splits = (int)fit;
+    if (splits >= 2) {
+      p.kps = (nk + splits - 1) / splits;
+      p.splits = (nk + p.kps - 1) / p.kps;  // every split non-empty
+      p.ws = ws;
+    }
+  }
+  p.tiles *= p.splits;
   constexpr int STAGE_BYTES = (TC_BM + BN) * TC_BK * 2;
   const int smem = TC_STAGES * STAGE_BYTES + 1024 + 256;
   auto kern = tc_gemm_kernel<T, ACT, MODE, BN>;
@@ -460,42 +544,55 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s) {
   const int grid = p.tiles < num_sms() ? p.tiles : num_sms();
   kern<<<grid, TC_THREADS, smem, s>>>(ta, tb, p);
   count_launch();
-  return check_launch("tcgen05 GEMM");
+  int rc2 = check_launch("tcgen05 GEMM");
+  if (rc2 || p.splits == 1) return rc2;
+  if constexpr (MODE == MODE_W || MODE == MODE_WD) {
+    const long long n4 = (long long)a.groups * a.Mg * a.Ng / 4;
+    long long blocks = (n4 + 255) / 256;
+    if (blocks > 148LL * 16) blocks = 148LL * 16;
+    ws_reduce_kernel<T, MODE><<<(int)blocks, 256, 0, s>>>(ws, p.splits, n4, a.out, a.scale, a.accumulate);
+    count_launch();
+    return check_launch("split-K reduce");
+  }
+  return IPC_OK;
 }
 
 template <typename T, int MODE, int BN>
-int dispatch_act(const GemmArgs& a, int act, int dtype, cudaStream_t s) {
+int dispatch_act(const GemmArgs& a, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes) {
   if constexpr (MODE == MODE_P || MODE == MODE_W || MODE == MODE_WD) {
-    return launch_tc_t<T, IPC_ACT_IDENTITY, MODE, BN>(a, dtype, s);  // activation only in I / F epilogues
+    return launch_tc_t<T, IPC_ACT_IDENTITY, MODE, BN>(a, dtype, s, ws, ws_bytes);  // f only in I / F epilogues
   } else {
-    IPC_DISPATCH_ACT(act, AC, { return launch_tc_t<T, AC, MODE, BN>(a, dtype, s); });
+    IPC_DISPATCH_ACT(act, AC, { return launch_tc_t<T, AC, MODE, BN>(a, dtype, s, ws, ws_bytes); });
   }
   return IPC_OK;
 }
 
 template <typename T, int BN>
-int dispatch_mode(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s) {
+int dispatch_mode(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes) {
   switch (mode) {
-    case MODE_P: return dispatch_act<T, MODE_P, BN>(a, act, dtype, s);
-    case MODE_I: return dispatch_act<T, MODE_I, BN>(a, act, dtype, s);
-    case MODE_W: return dispatch_act<T, MODE_W, BN>(a, act, dtype, s);
-    case MODE_WD: return dispatch_act<T, MODE_WD, BN>(a, act, dtype, s);
-    case MODE_F: return dispatch_act<T, MODE_F, BN>(a, act, dtype, s);
+    case MODE_P: return dispatch_act<T, MODE_P, BN>(a, act, dtype, s, ws, ws_bytes);
+    case MODE_I: return dispatch_act<T, MODE_I, BN>(a, act, dtype, s, ws, ws_bytes);
+    case MODE_W: return dispatch_act<T, MODE_W, BN>(a, act, dtype, s, ws, ws_bytes);
+    case MODE_WD: return dispatch_act<T, MODE_WD, BN>(a, act, dtype, s, ws, ws_bytes);
+    case MODE_F: return dispatch_act<T, MODE_F, BN>(a, act, dtype, s, ws, ws_bytes);
     default: return set_error(IPC_ERR_ARG, "bad GEMM mode %d", mode);
   }
 }
 
 }  // namespace
 
-bool tc_eligible(int mode, int M, int K, int B, int dtype, int algo, bool b_activated) {
+bool tc_eligible(int mode, int M, int K, int B, int dtype, int algo, bool b_activated, bool splitk) {
   if (algo != IPC_ALGO_AUTO && algo != IPC_ALGO_TCGEN05) return false;
   if (dtype != IPC_DT_F16 && dtype != IPC_DT_BF16) return false;
   if (b_activated) return false;  // f on the B operand is materialised once by the caller
   int Mg = M, Ng = B, Kg = K;
-  if (mode == MODE_W || mode == MODE_WD) { Ng = K; Kg = B; }
+  const bool weight = (mode == MODE_W || mode == MODE_WD);
+  if (weight) { Ng = K; Kg = B; }
   if (Mg < 1 || Ng < 1 || Kg < 1) return false;
   if (M % 8 || K % 8 || B % 8) return false;  // 16-byte row strides for TMA and the epilogue vectors
   if (algo == IPC_ALGO_AUTO) {
+    // a weight update with a long batch reduction spreads it over the SMs (split-K)
+    if (weight && splitk && Kg >= 1024 && Mg >= 16 && Ng >= 16) return true;
     // below ~128 x 256 x 256 the generic kernel's lower latency wins
     if (Mg < 128 || Ng < 128 || Kg < 64) return false;
     if ((double)Mg * Ng * Kg < 128.0 * 256 * 256) return false;
@@ -503,14 +600,17 @@ bool tc_eligible(int mode, int M, int K, int B, int dtype, int algo, bool b_acti
   return true;
 }
 
-int launch_tc(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s) {
+int launch_tc(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes) {
   if (a.Mg <= 0 || a.Ng <= 0 || a.groups <= 0) return IPC_OK;
   if (a.Kg <= 0) return launch_generic(a, mode, false, act, dtype, s);  // nothing to multiply
-  const bool wide = a.Ng >= 256;
+  // 128 x 256 tiles unless that leaves SMs idle and 128 x 128 tiles would not
+  const long long t256 = (long long)((a.Mg + TC_BM - 1) / TC_BM) * ((a.Ng + 255) / 256) * a.groups;
+  const bool wide = a.Ng >= 256 && t256 >= num_sms();
   if (dtype == IPC_DT_F16)
-    return wide ? dispatch_mode<__half, 256>(a, mode, act, dtype, s) : dispatch_mode<__half, 128>(a, mode, act, dtype, s);
-  return wide ? dispatch_mode<__nv_bfloat16, 256>(a, mode, act, dtype, s)
-              : dispatch_mode<__nv_bfloat16, 128>(a, mode, act, dtype, s);
+    return wide ? dispatch_mode<__half, 256>(a, mode, act, dtype, s, ws, ws_bytes)
+                : dispatch_mode<__half, 128>(a, mode, act, dtype, s, ws, ws_bytes);
+  return wide ? dispatch_mode<__nv_bfloat16, 256>(a, mode, act, dtype, s, ws, ws_bytes)
+              : dispatch_mode<__nv_bfloat16, 128>(a, mode, act, dtype, s, ws, ws_bytes);
 }
 
 int read_device_status(int* status, int clear) {

@@ -6,8 +6,12 @@ namespace ipc {
 // True when the tensor-core kernel serves this request: 16-bit storage, inner
 // dimensions multiples of 8, no activation to apply to the B operand, and (for
 // IPC_ALGO_AUTO) large enough to fill 128 x 256 tiles.
-bool tc_eligible(int mode, int M, int K, int B, int dtype, int algo, bool b_activated);
-int launch_tc(const GemmArgs& p, int mode, int act, int dtype, cudaStream_t s);
+// splitk: an fp32 workspace is available, so a weight update whose batch
+// reduction is long and whose output has few tiles may be split over the SMs.
+bool tc_eligible(int mode, int M, int K, int B, int dtype, int algo, bool b_activated, bool splitk = false);
+// ws / ws_bytes: optional fp32 workspace for split-K partial tiles (weight modes).
+int launch_tc(const GemmArgs& p, int mode, int act, int dtype, cudaStream_t s, float* ws = nullptr,
+              size_t ws_bytes = 0);
 // Device status word written by bounded waits (0 = fine); clear != 0 resets it.
 int read_device_status(int* status, int clear);
 }  // namespace ipc

@@ -134,6 +134,7 @@ class TileLangIPC:
         # activation cache of the 16-bit operator path: ac[l] = cast(f(x[l])), written by the forward
         # sweep and the state-update epilogues, read as the stored operand of P / W (tensor-core GEMMs)
         self._ac: list[torch.Tensor] | None = None
+        self._splitk_ws: torch.Tensor | None = None
         self._ac_grouped: list[torch.Tensor] = []
         self._runtime_plan_key: tuple | None = None
         self._pred_singleton_kernels: list[object | None] = []
@@ -216,6 +217,10 @@ class TileLangIPC:
         use_ac = self._acache_path(B)
         self._ac = [None] * len(dims) if use_ac else None  # type: ignore[list-item]
         self._ac_grouped = []
+        # fp32 scratch of the split-K weight update (narrow layers, long batches); shared by all layers,
+        # whose updates are ordered on one stream
+        self._splitk_ws = (torch.empty(N.SPLITK_WORKSPACE_BYTES // 4, device=dev, dtype=torch.float32)
+                           if use_ac else None)
         grouped_states = set()
         for gi, gr in enumerate(self._layer_groups):
             xbuf = torch.zeros((gr.state_count, gr.width, B), device=dev, dtype=dt)
@@ -252,9 +257,10 @@ class TileLangIPC:
                 and not self.net_kernel_eligible(B))
 
     def _fg(self, mode, a, b, out, aux=None, aux2=None, *, M, K, B, groups=1, scale=0.0, flags=0):
+        ws = self._splitk_ws if mode in (N.MODE_WEIGHT, N.MODE_WDELTA) else None
         N.fused_gemm(mode, a, b, out, aux, aux2, M=M, K=K, B=B, groups=groups, scale=scale, flags=flags,
                      act=self.cfg.activation, dtype=self.cfg.dtype, algo=getattr(self.cfg.kernel, "backend", "auto"),
-                     device=self.device)
+                     device=self.device, workspace=ws)
 
     def _prepare_runtime_plan(self, batch: int) -> None:
         """Build the kernel-call plan once per (dims, batch, activation, dtype, mode)."""
