@@ -175,6 +175,36 @@ int ipc_fused_gemm_ws(int mode, const void* a, const void* b, void* out, const v
                       int B, int groups, float scale, int flags, int act, int dtype, int algo, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/*
+ * Split-K weight update that allocates nothing: ipc_fused_gemm_ws for
+ * IPC_MODE_WEIGHT / IPC_MODE_WDELTA (same operands, flags, act, algo) with
+ * the fp32 partial tiles in a scratch array compiled into this library,
+ * IPC_NOALLOC_SCRATCH_BYTES per device, instead of caller memory.  For
+ * callers that hold no device allocator of their own: a host runtime bound
+ * over the C ABI (cgo, JNI, ctypes) that was handed only the operand buffers
+ * and must not cudaMalloc behind the back of the framework that owns the
+ * device memory (a caching allocator that does not see such memory can run
+ * the device out of it), or a step that runs under a fixed memory budget.
+ *   - Limit: groups*M*K <= IPC_NOALLOC_MAX_OUT_ELEMS; larger requests return
+ *     IPC_ERR_ARG (use ipc_fused_gemm_ws with a caller workspace instead).
+ *     Within the limit the split count equals ipc_fused_gemm_ws with a
+ *     16 MiB workspace.  Other modes return IPC_ERR_ARG.
+ *   - Nothing in the scratch has to start at zero: every partial tile is
+ *     written before the reduce pass reads it.
+ *   - The scratch is one array per device, shared by every caller in the
+ *     process: calls on one device whose kernels can overlap (different
+ *     streams, or host threads without ordering) race on it.  Order them on
+ *     one stream.
+ *   - The first call on each device does set-up (looks up the scratch
+ *     address with cudaGetSymbolAddress, with that device current); make it
+ *     before any stream capture.
+ * No counterpart in the reference.
+ */
+#define IPC_NOALLOC_SCRATCH_BYTES (16u << 20)
+#define IPC_NOALLOC_MAX_OUT_ELEMS (1u << 20)
+int ipc_weight_update_noalloc(int mode, const void* e, const void* a_up, void* out, int M, int K, int B, int groups,
+                              float alpha, int flags, int act, int dtype, int algo, void* stream);
+
 /* First error a device-side bounded wait recorded since the last clear
  * (IPC_OK if none; IPC_ERR_TIMEOUT when a pipeline wait gave up).  Synchronises
  * with the device; clear != 0 resets the word.  No reference counterpart. */

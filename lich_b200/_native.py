@@ -44,7 +44,7 @@ EXPORTED = (
     "ipc_abi_version", "ipc_last_error", "ipc_launch_count", "ipc_pred_err", "ipc_pred_err_saved",
     "ipc_forward", "ipc_infer_update", "ipc_weight_update", "ipc_weight_delta", "ipc_weight_apply",
     "ipc_activate", "ipc_net_train", "ipc_net_plan", "ipc_fused_gemm", "ipc_device_status",
-    "ipc_fused_gemm_ws",
+    "ipc_fused_gemm_ws", "ipc_weight_update_noalloc",
 )
 
 
@@ -119,6 +119,7 @@ def load() -> ctypes.CDLL:
         "ipc_fused_gemm": (i, [i, vp, vp, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp]),
         "ipc_device_status": (i, [POINTER(c_int), i]),
         "ipc_fused_gemm_ws": (i, [i, vp, vp, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp, c_size_t, vp]),
+        "ipc_weight_update_noalloc": (i, [i, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
