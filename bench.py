@@ -484,6 +484,308 @@ def run_c5(args, world, rank, local):
     return line
 
 
+C4B_DIMS = (10, 64, 64, 64, 784)
+C4B_NETS = 4096
+
+
+def run_c4b(args, world, rank, local):
+    """configs[3] batched form: 4096 independent networks, dims (10,64x3,784), B=128 each, bf16, tanh, T=4.
+
+    The networks are split over the ranks with no communication (``many_nets.shard``); one launch of the
+    persistent kernel trains every network of a rank for a chunk of steps (``ManyNetIPC.train_pool``).
+    Network n starts from N(0, 1/fan_in) weights of seed 1 + n; batches come from a resident device pool of
+    two batches per network (1.6 GB at 4096 networks, larger than L2)."""
+    from lich_b200 import _native as N
+    from lich_b200 import synthetic as S
+    from lich_b200.many_nets import ManyNetIPC, shard
+    from lich_b200.trainer import IPCConfig
+
+    dev = torch.device("cuda", local)
+    dtype, B, T, dims = torch.bfloat16, 128, 4, C4B_DIMS
+    total = args.nets or C4B_NETS
+    mine = shard(total, world, rank)
+    nets = len(mine)
+    cfg = IPCConfig(dims=dims, alpha=1e-4, gamma=0.5, activation=args.act, dtype=dtype)
+    model = ManyNetIPC(cfg, nets, B, device=dev)
+    w_host = [S.fan_in_normal(dims, seed=1 + n) for n in mine]
+    for l in range(len(dims) - 1):
+        model.w[l].copy_(torch.stack([w[l] for w in w_host]).to(dev, dtype))
+    del w_host
+    w_init = [w.clone() for w in model.w]
+    P = 2
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    pool_x = torch.rand((P, nets, dims[-1], B), generator=g, device=dev).to(dtype)
+    pool_y = torch.zeros((P, nets, dims[0], B), device=dev, dtype=dtype)
+    pool_y.scatter_(2, torch.randint(0, dims[0], (P, nets, 1, B), generator=g, device=dev), 1.0)
+
+    def restore():
+        for w, w0 in zip(model.w, w_init):
+            w.copy_(w0)
+
+    # pick the cluster size among the plans that fit (at B=128 only 8 CTAs x 16 columns does today)
+    # by a short untimed run of each
+    stream = torch.cuda.current_stream(dev)
+    tried = {}
+    for c in (8, 4):
+        if N.net_plan(dims, B, nets=nets, cluster=c) is None:
+            continue
+        model.cluster = c
+        model.train_pool(pool_x, pool_y, steps=1, T=T)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        model.train_pool(pool_x, pool_y, steps=4, T=T)
+        b.record(stream)
+        b.synchronize()
+        tried[c] = a.elapsed_time(b) / 4
+    model.cluster = min(tried, key=tried.get)
+    restore()
+    model.train_pool(pool_x, pool_y, steps=max(args.warmup, 1), T=T)
+    torch.cuda.synchronize(dev)
+
+    chunk = max(1, min(args.chunk, args.steps, RESET_EVERY))
+    launches0 = N.launch_count()
+    evs = []
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        done = 0
+        while done < args.steps:
+            n = min(chunk, args.steps - done)
+            if done % RESET_EVERY == 0:
+                restore()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            model.train_pool(pool_x, pool_y, steps=n, T=T, first_batch=done % P)
+            e1.record(stream)
+            evs.append((e0, e1, n))
+            done += n
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    launches = N.launch_count() - launches0
+    ms = max_over_ranks(start.elapsed_time(end), world, dev)
+    assert all(torch.isfinite(w).all() for w in model.w)
+
+    flop_net, bytes_net = step_costs(dims, B, T, 2)
+    pk = peaks()
+    full = [(a.elapsed_time(b), n) for a, b, n in evs if n == chunk] or [(a.elapsed_time(b), n) for a, b, n in evs]
+    avg_ms = sum(t for t, _ in full) / len(full)
+    units = full[0][1] * nets  # network-steps per launch
+    tfs = flop_net * units / (avg_ms * 1e-3) / 1e12
+    # HBM the fused step cannot avoid: each network-step reads its batch (x_L and the one-hot target)
+    need_net = (dims[-1] + dims[0]) * B * 2
+    need_gbs = need_net * units / (avg_ms * 1e-3) / 1e9
+    roof = {"bound": "tensor", "achieved": round(tfs, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": round(tfs / pk["bf16_tflops"], 4),
+            "traffic": TRAFFIC_PER_STEP.get(("c4b", 1)) and round(TRAFFIC_PER_STEP[("c4b", 1)] * units),
+            "peak_source": pk["source"], "kernel": "net_kernel (ipc_net_train, nets per launch = %d)" % nets,
+            "algorithmic_flop_per_network_step": flop_net, "network_steps_per_launch": units,
+            "avg_launch_ms": round(avg_ms, 4),
+            "operator_bytes_per_network_step": bytes_net,
+            "operator_bytes_gbs": round(bytes_net * units / (avg_ms * 1e-3) / 1e9, 1),
+            "batch_bytes_per_network_step": need_net, "batch_read_gbs": round(need_gbs, 1),
+            "batch_read_frac_of_hbm": round(need_gbs / pk["hbm_gbs"], 4),
+            "cluster": model.cluster, "cluster_trial_ms_per_step": {str(k): round(v, 4) for k, v in tried.items()}}
+
+    # e2e: batches in pinned host memory, copied every step (copy stream, double-buffered), energy read back
+    n_e2e = max(2, min(args.steps, 8))
+    x_h = pool_x[0].cpu().pin_memory()
+    y_h = pool_y[0].cpu().pin_memory()
+    ring = [(torch.empty_like(pool_x[:1]), torch.empty_like(pool_y[:1])) for _ in range(2)]
+    energy = torch.empty(2, nets, device=dev, dtype=torch.float32)
+    energy_h = torch.empty(n_e2e, nets, dtype=torch.float32).pin_memory()
+    copy = torch.cuda.Stream(dev)
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    for s_ in range(2):
+        free[s_].record(stream)
+    restore()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+
+    def h2d(slot):
+        with torch.cuda.stream(copy):
+            copy.wait_event(free[slot])
+            ring[slot][0][0].copy_(x_h, non_blocking=True)
+            ring[slot][1][0].copy_(y_h, non_blocking=True)
+            ready[slot].record(copy)
+
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    h2d(0)
+    for i in range(n_e2e):
+        slot = i % 2
+        if i + 1 < n_e2e:
+            h2d((i + 1) % 2)
+        stream.wait_event(ready[slot])
+        model.train_pool(ring[slot][0], ring[slot][1], steps=1, T=T, energy=energy[slot])
+        energy_h[i].copy_(energy[slot], non_blocking=True)
+        free[slot].record(stream)
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1), world, dev)
+    assert torch.isfinite(energy_h).all()
+
+    line = {
+        "metric": METRIC, "value": round(total * B * args.steps / (ms * 1e-3), 1), "unit": "samples/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"configs[3] batched: {total} independent networks, dims (10,64x3,784), B=128 each, "
+                               f"T=4, {args.act}, bf16 storage / fp32 accumulation, alpha 1e-4, gamma 0.5",
+                   "networks": total, "networks_per_rank": nets, "batch": B, "T": T,
+                   "parallelism": f"shards{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2: two resident batches per network (1.6 GB at 4096 networks)",
+                   "steps_per_launch": chunk},
+        "roofline": roof,
+        "e2e": {"value": round(total * B * n_e2e / (ms_e2e * 1e-3), 1), "unit": "samples/s",
+                "h2d_bytes_per_step": int(x_h.numel() + y_h.numel()) * 2, "d2h_bytes_per_step": 4 * nets,
+                "steps": n_e2e,
+                "path": "ManyNetIPC.train_pool one step per launch on batches copied from pinned host memory "
+                        "(copy stream, double-buffered), per-network energy read back"},
+        "gpu_launches": int(launches), "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(dims, B, T, args.act)
+        line["cpu_baseline"]["sample"] += " (one network; the host trains networks one after another)"
+    return line
+
+
+C4A_DIMS = (10, 1024, 1024, 1024, 1024, 784)
+C4A_BATCHES = (1, 4, 16)
+
+
+def _c4a_point(dims, B, T, steps, warmup, dev, chunk):
+    """Time `steps` training steps (fresh batch each, forward sweep + T iterations + W) at batch B:
+    CUDA graphs of `chunk` steps over a device pool, replayed."""
+    from lich_b200 import _native as N
+    from lich_b200 import synthetic as S
+    from lich_b200.trainer import IPCConfig, TileLangIPC
+
+    dtype = torch.bfloat16
+    cfg = IPCConfig(dims=dims, alpha=1e-4, gamma=0.5, activation="tanh", dtype=dtype)
+    model = TileLangIPC(cfg, device=dev)
+    for dst, src in zip(model.w, S.fan_in_normal(dims, seed=1)):
+        dst.copy_(src.to(dev, dtype))
+    w_init = [w.clone() for w in model.w]
+    # pool of chunk batches (x is tiny at B <= 16; L2 holds it, the weights -- 8.4 MB -- are re-read every phase)
+    g = torch.Generator(device=dev).manual_seed(5)
+    px = torch.rand((chunk, dims[-1], B), generator=g, device=dev).to(dtype)
+    py = torch.zeros((chunk, dims[0], B), device=dev, dtype=dtype)
+    py.scatter_(1, torch.randint(0, dims[0], (chunk, 1, B), generator=g, device=dev), 1.0)
+    for b in range(chunk):  # eager pass: every kernel's one-time setup outside the capture
+        model.train_step(px[b], py[b], T=T)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for b in range(chunk):
+            model.train_step(px[b], py[b], T=T)
+    torch.cuda.synchronize(dev)
+    for _ in range(max(1, warmup // chunk)):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    reps = max(1, steps // chunk)
+    stream = torch.cuda.current_stream(dev)
+    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for r in range(reps):
+        if (r * chunk) % RESET_EVERY == 0:
+            for w, w0 in zip(model.w, w_init):
+                w.copy_(w0)
+        graph.replay()
+    b_.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b_)
+    # graph replays bypass the library's launch counter: count one eager step for the per-step figure
+    n0 = N.launch_count()
+    model.train_step(px[0], py[0], T=T)
+    torch.cuda.synchronize(dev)
+    per_step_launches = N.launch_count() - n0
+    assert all(torch.isfinite(w).all() for w in model.w)
+    del graph
+    return {"B": B, "steps": reps * chunk, "ms": ms, "ms_per_step": ms / (reps * chunk),
+            "launches_per_step": per_step_launches, "model": model, "pool": (px, py),
+            "gpu_launches": per_step_launches * reps * chunk}
+
+
+def run_c4a(args, world, rank, local):
+    """configs[3] small-batch path: dims (10,1024x4,784), B in {1,4,16}, T=8, bf16, tanh, alpha 1e-4.
+
+    P and I run the mma.sync kernel (N = B columns), W runs the outer-product kernel (B <= 16, the
+    specialisation the config exercises).  The headline is B=16 (``--batch`` picks another); every B of the
+    config is reported under ``points``.  Replicas only: ``--gpus N`` runs N independent copies."""
+    from lich_b200 import _native as N
+    dev = torch.device("cuda", local)
+    dims, T = C4A_DIMS, 8
+    head_b = args.batch or 16
+    pk = peaks()
+    points, head = [], None
+    chunk = max(1, min(args.chunk, 50))
+    barrier(world)
+    with ClockSampler(local) as clk:
+        for B in sorted(set(C4A_BATCHES) | {head_b}):
+            r = _c4a_point(dims, B, T, args.steps, args.warmup, dev, chunk)
+            flop, nbytes = step_costs(dims, B, T, 2)
+            gbs = nbytes / (r["ms_per_step"] * 1e-3) / 1e9
+            pt = {"B": B, "ms_per_step": round(r["ms_per_step"], 5), "samples_per_s": round(B / (r["ms_per_step"] * 1e-3), 1),
+                  "algorithmic_bytes_per_step": nbytes, "algorithmic_flop_per_step": flop, "gbs": round(gbs, 1),
+                  "frac_hbm": round(gbs / pk["hbm_gbs"], 4), "launches_per_step": r["launches_per_step"]}
+            points.append(pt)
+            if B == head_b:
+                head = (r, pt)
+            else:
+                del r
+            torch.cuda.empty_cache()
+    r, pt = head
+    ms_max = max_over_ranks(r["ms"], world, dev)
+    steps = r["steps"]
+    model = r["model"]
+    px, py = r["pool"]
+    # e2e: the public call (TileLangIPC.train_step) per step on a batch copied from pinned host memory,
+    # the step's energy read back
+    x_h = px[0].cpu().pin_memory()
+    y_h = py[0].cpu().pin_memory()
+    xd, yd = torch.empty_like(px[0]), torch.empty_like(py[0])
+    n_e2e = max(10, min(args.steps, 200))
+    m_h = torch.empty(n_e2e, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize(dev)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for i in range(n_e2e):
+        xd.copy_(x_h, non_blocking=True)
+        yd.copy_(y_h, non_blocking=True)
+        model.train_step(xd, yd, T=T)
+        m_h[i:i + 1].copy_((model.e[0].float() ** 2).mean().reshape(1), non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1), world, dev)
+    B = head_b
+    line = {
+        "metric": METRIC, "value": round(world * steps * B / (ms_max * 1e-3), 1), "unit": "samples/s",
+        "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms_max / steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"configs[3] small batch: dims (10,1024x4,784), B={B}, T=8, tanh, bf16 storage / "
+                               f"fp32 accumulation, alpha 1e-4, gamma 0.5", "batch": B, "T": T,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "weights (8.4 MB) stay in L2 between phases; no flush (the step re-reads them 80 times)",
+                   "graph_steps": chunk},
+        "roofline": {"bound": "hbm", "achieved": pt["gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": pt["frac_hbm"], "traffic": None, "peak_source": pk["source"],
+                     "kernel": "whole step (mma.sync P / I, outer-product W, forward sweep) under one CUDA graph",
+                     "algorithmic_bytes_per_step": pt["algorithmic_bytes_per_step"]},
+        "points": points,
+        "e2e": {"value": round(world * n_e2e * B / (ms_e2e * 1e-3), 1), "unit": "samples/s",
+                "h2d_bytes_per_step": int(x_h.numel() + y_h.numel()) * 2, "d2h_bytes_per_step": 4, "steps": n_e2e,
+                "path": "TileLangIPC.train_step (eager launches) on a batch copied from pinned host memory"},
+        "gpu_launches": int(r["gpu_launches"]), "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(dims, B, T, "tanh", budget_s=12.0)
+    return line
+
+
 C3_SIZES = (64, 256, 1024, 4096, 8192)
 C3_BATCHES = (128, 1024, 8192, 65536)
 
@@ -595,6 +897,23 @@ def run_reference(args, world, rank):
                 "cpu_baseline": cb,
                 "e2e": {"value": round(cb["value"], 1), "unit": "samples/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
+    if args.config in ("c4a", "c4b"):
+        if args.config == "c4a":
+            dims, B, T, scaling = C4A_DIMS, args.batch or 16, 8, "weak"
+            wl = f"configs[3] small batch: dims (10,1024x4,784), B={B}, T=8, tanh"
+        else:
+            dims, B, T, scaling = C4B_DIMS, 128, 4, "strong"
+            wl = (f"configs[3] batched: {args.nets or C4B_NETS} networks of dims (10,64x3,784), B=128, T=4, "
+                  f"{args.act} (the host trains them one after another; sample: one network)")
+        cb = cpu_baseline(dims, B, T, "tanh" if args.config == "c4a" else args.act,
+                          budget_s=max(10.0, min(120.0, 0.01 * args.steps + 5.0)))
+        return {"metric": METRIC, "value": round(cb["value"], 1), "unit": "samples/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(B / cb["value"] * 1e3, 4),
+                "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "impl": "reference", "config": {"workload": wl, "batch": B, "T": T},
+                "cpu_baseline": cb,
+                "e2e": {"value": round(cb["value"], 1), "unit": "samples/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
     dims = S.paper_dims(args.depth)
     B, T = 128, 4
     budget = max(5.0, min(120.0, 0.005 * args.steps + 2.0))
@@ -616,12 +935,14 @@ def main():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c3", "c5"], default="c2",
+    ap.add_argument("--config", choices=["c2", "c3", "c4a", "c4b", "c5"], default="c2",
                     help="c2: configs[1] hidden-64 (default); c3: configs[2] per-kernel microbench; "
+                         "c4a: configs[3] small batch; c4b: configs[3] 4096 networks; "
                          "c5: configs[4] wide data-parallel")
+    ap.add_argument("--nets", type=int, default=0, help="c4b: number of networks (default 4096)")
     ap.add_argument("--sizes", default="", help="c3: comma-separated M=K list")
     ap.add_argument("--batches", default="", help="c3: comma-separated B list")
-    ap.add_argument("--batch", type=int, default=0, help="c5: global batch (default 65536)")
+    ap.add_argument("--batch", type=int, default=0, help="c5: global batch (default 65536); c4a: headline B")
     ap.add_argument("--depth", type=int, default=6)
     ap.add_argument("--act", default="tanh")
     ap.add_argument("--chunk", type=int, default=500, help="training steps per persistent-kernel launch")
@@ -635,10 +956,12 @@ def main():
         if line is not None:
             print(json.dumps(line), flush=True)
         return
-    if args.config == "c5" and "--steps" not in sys.argv:
-        args.steps = 5
+    if "--steps" not in sys.argv:
+        args.steps = {"c5": 5, "c4b": 200, "c4a": 500}.get(args.config, args.steps)
+    if args.config == "c4b" and "--chunk" not in sys.argv:
+        args.chunk = 50
     world, rank, local = dist_setup(args)
-    runners = {"c2": run_c2, "c3": run_c3, "c5": run_c5}
+    runners = {"c2": run_c2, "c3": run_c3, "c4a": run_c4a, "c4b": run_c4b, "c5": run_c5}
     line = runners[args.config](args, world, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -93,6 +93,7 @@ static int pred_err_impl(const void* x_up, const void* w, const void* x_lo, void
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (tc_eligible(MODE_P, M, K, B, dtype, algo, bact)) return launch_tc(p, MODE_P, act, dtype, s);
   if (algo == IPC_ALGO_TCGEN05) return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: shape/dtype not eligible (M=%d K=%d B=%d dtype=%d)", M, K, B, dtype);
+  if (skinny_eligible(MODE_P, M, K, B, dtype, algo)) return launch_skinny(p, MODE_P, bact, act, dtype, s);
   return launch_generic(p, MODE_P, bact, act, dtype, s);
 }
 
@@ -121,6 +122,7 @@ int ipc_forward(const void* x_up, const void* w, void* out, int M, int K, int B,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (tc_eligible(MODE_F, M, K, B, dtype, algo, true)) return launch_tc(p, MODE_F, act, dtype, s);
   if (algo == IPC_ALGO_TCGEN05) return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: shape/dtype not eligible (M=%d K=%d B=%d dtype=%d)", M, K, B, dtype);
+  if (skinny_eligible(MODE_F, M, K, B, dtype, algo)) return launch_skinny(p, MODE_F, true, act, dtype, s);
   return launch_generic(p, MODE_F, true, act, dtype, s);
 }
 
@@ -142,6 +144,7 @@ int ipc_infer_update(void* x, const void* e, const void* w_low, const void* e_lo
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (tc_eligible(MODE_I, M, K, B, dtype, algo, false)) return launch_tc(p, MODE_I, act, dtype, s);
   if (algo == IPC_ALGO_TCGEN05) return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: shape/dtype not eligible (M=%d K=%d B=%d dtype=%d)", M, K, B, dtype);
+  if (skinny_eligible(MODE_I, M, K, B, dtype, algo)) return launch_skinny(p, MODE_I, false, act, dtype, s);
   return launch_generic(p, MODE_I, false, act, dtype, s);
 }
 
@@ -238,6 +241,7 @@ static int fused_gemm_impl(int mode, const void* a, const void* b, void* out, co
   if (algo == IPC_ALGO_TCGEN05)
     return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: not eligible (mode=%d M=%d K=%d B=%d dtype=%d activate_b=%d)",
                      mode, M, K, B, dtype, (int)bact);
+  if (skinny_eligible(mode, M, K, B, dtype, algo)) return launch_skinny(p, mode, bact, act, dtype, s);
   return launch_generic(p, mode, bact, act, dtype, s);
 }
 

@@ -30,4 +30,9 @@ struct GemmArgs {
 
 int launch_generic(const GemmArgs& p, int mode, bool bact, int act, int dtype, cudaStream_t s);
 
+// Small-batch path of P / I / F (N = B <= 16, 16-bit storage, IPC_ALGO_AUTO): a cluster of CTAs per
+// 16 output rows splits K and reduces over distributed shared memory (ipc_skinny.cu).
+bool skinny_eligible(int mode, int M, int K, int B, int dtype, int algo);
+int launch_skinny(const GemmArgs& p, int mode, bool bact, int act, int dtype, cudaStream_t s);
+
 }  // namespace ipc
