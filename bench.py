@@ -724,7 +724,8 @@ def run_c4a(args, world, rank, local):
     chunk = max(1, min(args.chunk, 50))
     barrier(world)
     with ClockSampler(local) as clk:
-        for B in sorted(set(C4A_BATCHES) | {head_b}):
+        batches = [int(b) for b in args.batches.split(",")] if args.batches else list(C4A_BATCHES)
+        for B in sorted(set(batches) | {head_b}):
             r = _c4a_point(dims, B, T, args.steps, args.warmup, dev, chunk)
             flop, nbytes = step_costs(dims, B, T, 2)
             gbs = nbytes / (r["ms_per_step"] * 1e-3) / 1e9
@@ -941,7 +942,7 @@ def main():
                          "c5: configs[4] wide data-parallel")
     ap.add_argument("--nets", type=int, default=0, help="c4b: number of networks (default 4096)")
     ap.add_argument("--sizes", default="", help="c3: comma-separated M=K list")
-    ap.add_argument("--batches", default="", help="c3: comma-separated B list")
+    ap.add_argument("--batches", default="", help="c3 / c4a: comma-separated B list")
     ap.add_argument("--batch", type=int, default=0, help="c5: global batch (default 65536); c4a: headline B")
     ap.add_argument("--depth", type=int, default=6)
     ap.add_argument("--act", default="tanh")
