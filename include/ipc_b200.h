@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define IPC_ABI_VERSION 1
+#define IPC_ABI_VERSION 2
 
 /* return codes */
 #define IPC_OK 0
@@ -210,6 +210,14 @@ int ipc_weight_update_noalloc(int mode, const void* e, const void* a_up, void* o
  * with the device; clear != 0 resets the word.  No reference counterpart. */
 int ipc_device_status(int* status, int clear);
 
+/* Failure-detection self-test of the bounded device waits: launches a 2-CTA
+ * kernel in which one CTA never reaches the grid barrier used by the wide
+ * small-batch kernel; the other gives up after limit_us microseconds (1 ..
+ * 1e6), records IPC_ERR_TIMEOUT in the device status (ipc_device_status) and
+ * returns.  Nothing faults and the context stays usable.  sync:
+ * IPC_NET_SYNC_BYTES of device memory.  No reference counterpart. */
+int ipc_selftest_barrier_timeout(void* sync, int limit_us, void* stream);
+
 /* A = cast(f(X)) over n elements (materialise a saved activation). */
 int ipc_activate(void* a, const void* x, long long n, int act, int dtype, void* stream);
 
@@ -226,9 +234,14 @@ int ipc_activate(void* a, const void* x, long long n, int act, int dtype, void* 
  * of the last iteration and the updated states (reference.py:52-57).
  * With pool == NULL, forward_init == 0, T == 1 and update_weights == 1 a call
  * is exactly TileLangIPC.step_initialized (trainer.py:601-679).
- * Limits: 1 <= L <= IPC_NET_MAX_LAYERS; d_0 .. d_{L-1} <= 64; d_L a multiple
- * of 8; B a multiple of 8 and <= 256; 16-bit storage; the per-CTA layout must
- * fit in shared memory (ipc_net_plan answers).
+ * Two kernels serve it (ipc_net_plan answers which, and whether either can):
+ *  - small widths: d_0 .. d_{L-1} <= 64, d_L a multiple of 8, B a multiple of
+ *    8 and <= 256, the per-CTA layout fits in shared memory; one cluster of
+ *    CTAs per network, any number of networks (nets);
+ *  - wide networks at small batch (everything else with 1 <= B <= 16, every
+ *    d_l <= 4096, nets == 1): one cooperative grid, one CTA per SM, phases
+ *    separated by bounded grid barriers; needs run->sync.
+ * Both: 1 <= L <= IPC_NET_MAX_LAYERS, 16-bit storage, recompute mode.
  * --------------------------------------------------------------------------- */
 #define IPC_NET_MAX_LAYERS 8
 
@@ -240,6 +253,9 @@ typedef struct ipc_net {
   void* w[IPC_NET_MAX_LAYERS];      /* W[l]: [nets, d_l, d_{l+1}] */
   void* x[IPC_NET_MAX_LAYERS + 1];  /* x[l]: [nets, d_l, B] */
   void* e[IPC_NET_MAX_LAYERS + 1];  /* e[l]: [nets, d_l, B] (e[L] unused, may be NULL) */
+  void* a[IPC_NET_MAX_LAYERS + 1];  /* optional activation cache a[l] = cast(f(x[l])), [nets, d_l, B],
+                                       l >= 1, used by the wide small-batch kernel (contents on
+                                       entry ignored; NULL entries: f is recomputed where read) */
 } ipc_net_t;
 
 typedef struct ipc_net_run {
@@ -259,8 +275,15 @@ typedef struct ipc_net_run {
                          each step (reference.py:58); zeroed by the call */
   long long* phase_ns; /* [min(steps, IPC_NET_TRACE_STEPS), IPC_NET_TRACE_PHASES] or NULL:
                           %globaltimer stamps (ns) taken by CTA 0 of network 0 at the end of
-                          each phase of a step (tracing; no work is skipped) */
+                          each phase of a step (tracing; no work is skipped).  The wide
+                          small-batch kernel fills slots 0-6: step start, batch ready,
+                          forward sweep done, first P, first I, last iteration, weights */
+  void* sync;         /* IPC_NET_SYNC_BYTES of device memory for the grid barrier of the
+                         wide small-batch kernel (zeroed by the call; one per launch in
+                         flight); NULL for the small-width kernel */
 } ipc_net_run_t;
+
+#define IPC_NET_SYNC_BYTES 64
 
 #define IPC_NET_TRACE_STEPS 64
 #define IPC_NET_TRACE_PHASES 12 /* start, mu-partial, barrier A, mu-sum, forward, iterations,
@@ -268,8 +291,9 @@ typedef struct ipc_net_run {
                                    batch ready, end */
 
 /* Whether ipc_net_train can run this network: IPC_OK and the cluster size
- * (CTAs per network) and dynamic shared memory per CTA it would use, or an
- * IPC_ERR_* code.  cluster = 0 lets the library choose.  Launches nothing.
+ * (CTAs per network; 0 for the wide small-batch kernel, whose grid is one
+ * CTA per SM) and dynamic shared memory per CTA it would use, or an IPC_ERR_*
+ * code.  cluster = 0 lets the library choose.  Launches nothing.
  * No reference counterpart (a planning query of the persistent kernel). */
 int ipc_net_plan(const ipc_net_t* net, int cluster, int* cluster_out, int* smem_bytes_out);
 

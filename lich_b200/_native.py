@@ -39,12 +39,13 @@ SPLITK_WORKSPACE_BYTES = 16 << 20
 NET_MAX_LAYERS = 8
 NET_TRACE_STEPS = 64
 NET_TRACE_PHASES = 12
+NET_SYNC_BYTES = 64
 
 EXPORTED = (
     "ipc_abi_version", "ipc_last_error", "ipc_launch_count", "ipc_pred_err", "ipc_pred_err_saved",
     "ipc_forward", "ipc_infer_update", "ipc_weight_update", "ipc_weight_delta", "ipc_weight_apply",
     "ipc_activate", "ipc_net_train", "ipc_net_plan", "ipc_fused_gemm", "ipc_device_status",
-    "ipc_fused_gemm_ws", "ipc_weight_update_noalloc",
+    "ipc_fused_gemm_ws", "ipc_weight_update_noalloc", "ipc_selftest_barrier_timeout",
 )
 
 
@@ -57,6 +58,7 @@ class IpcNet(Structure):
         ("w", c_void_p * NET_MAX_LAYERS),
         ("x", c_void_p * (NET_MAX_LAYERS + 1)),
         ("e", c_void_p * (NET_MAX_LAYERS + 1)),
+        ("a", c_void_p * (NET_MAX_LAYERS + 1)),
     ]
 
 
@@ -78,6 +80,7 @@ class IpcNetRun(Structure):
         ("cluster", c_int),
         ("energy", c_void_p),
         ("phase_ns", c_void_p),
+        ("sync", c_void_p),
     ]
 
 
@@ -120,6 +123,7 @@ def load() -> ctypes.CDLL:
         "ipc_device_status": (i, [POINTER(c_int), i]),
         "ipc_fused_gemm_ws": (i, [i, vp, vp, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp, c_size_t, vp]),
         "ipc_weight_update_noalloc": (i, [i, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp]),
+        "ipc_selftest_barrier_timeout": (i, [vp, i, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -70,7 +70,9 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
     objs = [OBJ / (s.stem + ".o") for s in srcs]
     if todo or not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs)]
+        # --no-undefined: a symbol missing at link time is a build error, not a dlopen failure later
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-Xlinker", "--no-undefined", "-o", str(tmp),
+               *map(str, objs)]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)

@@ -260,10 +260,22 @@ int ipc_fused_gemm_ws(int mode, const void* a, const void* b, void* out, const v
                          static_cast<float*>(workspace), workspace_bytes, stream);
 }
 
+int ipc_selftest_barrier_timeout(void* sync, int limit_us, void* stream) {
+  int rc = require_sm100();
+  if (rc) return rc;
+  return wide_selftest_timeout(sync, limit_us, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int ipc_device_status(int* status, int clear) {
   int rc = require_sm100();
   if (rc) return rc;
-  return read_device_status(status, clear);
+  int tc = 0, wide = 0;
+  rc = read_device_status(&tc, clear);
+  if (rc) return rc;
+  rc = read_wide_status(&wide, clear);
+  if (rc) return rc;
+  if (status) *status = tc != 0 ? tc : wide;
+  return IPC_OK;
 }
 
 }  // extern "C"

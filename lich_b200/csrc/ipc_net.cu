@@ -784,8 +784,20 @@ int check_net(const ipc_net_t* net) {
 
 using namespace ipc;
 
+namespace ipc {
+// The wide small-batch step kernel (ipc_widenet.cu): networks the cluster kernel cannot hold.
+bool wide_net_fits(const ipc_net_t* net);
+int wide_net_smem(const ipc_net_t* net);
+int wide_net_train(const ipc_net_t* net, const ipc_net_run_t* run, cudaStream_t s);
+}  // namespace ipc
+
 extern "C" int ipc_net_plan(const ipc_net_t* net, int cluster, int* cluster_out, int* smem_bytes_out) {
   int rc = check_net(net);
+  if (rc == IPC_ERR_UNSUPPORTED && wide_net_fits(net)) {
+    if (cluster_out) *cluster_out = 0;  // one cooperative grid per network
+    if (smem_bytes_out) *smem_bytes_out = wide_net_smem(net);
+    return IPC_OK;
+  }
   if (rc) return rc;
   NetParams<__half> p;
   fill_params(p, net);
@@ -800,6 +812,8 @@ extern "C" int ipc_net_plan(const ipc_net_t* net, int cluster, int* cluster_out,
 extern "C" int ipc_net_train(const ipc_net_t* net, const ipc_net_run_t* run, void* stream) {
   if (net == nullptr || run == nullptr) return set_error(IPC_ERR_ARG, "null net / run descriptor");
   int rc = check_net(net);
+  const bool wide = (rc == IPC_ERR_UNSUPPORTED && wide_net_fits(net));
+  if (wide) rc = IPC_OK;
   if (rc) return rc;
   const int L = net->L;
   for (int l = 0; l < L; ++l)
@@ -821,6 +835,7 @@ extern "C" int ipc_net_train(const ipc_net_t* net, const ipc_net_run_t* run, voi
     cudaError_t err = cudaMemsetAsync(run->energy, 0, sizeof(float) * (size_t)run->steps * net->nets, s);
     if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "energy memset: %s", cudaGetErrorString(err));
   }
+  if (wide) return wide_net_train(net, run, s);
   IPC_DISPATCH_DT16(run->dtype, TT, { return run_net<TT>(net, run, s); });
   return IPC_OK;
 }

@@ -135,6 +135,8 @@ class TileLangIPC:
         # sweep and the state-update epilogues, read as the stored operand of P / W (tensor-core GEMMs)
         self._ac: list[torch.Tensor] | None = None
         self._splitk_ws: torch.Tensor | None = None
+        self._net_sync: torch.Tensor | None = None
+        self._net_acache: list | None = None
         self._ac_grouped: list[torch.Tensor] = []
         self._runtime_plan_key: tuple | None = None
         self._pred_singleton_kernels: list[object | None] = []
@@ -180,11 +182,13 @@ class TileLangIPC:
         """Whether ``step_initialized`` / ``train_pool`` run as one persistent-kernel launch."""
         d = self.cfg.dims
         ok = (self.cfg.use_net_kernel and self.cfg.dtype in (torch.float16, torch.bfloat16)
-              and self.recompute_activation and 1 <= self.L <= N.NET_MAX_LAYERS
-              and all(int(v) <= 64 for v in d[:-1]))
-        if batch is not None and ok:
-            ok = N.net_plan(d, int(batch), 1, int(self.cfg.net_cluster)) is not None
-        return bool(ok)
+              and self.recompute_activation and 1 <= self.L <= N.NET_MAX_LAYERS)
+        if not ok:
+            return False
+        if batch is None:  # without a batch size: whether the small-width (cluster) kernel applies
+            return all(int(v) <= 64 for v in d[:-1])
+        # small widths: one cluster per network; wide layers at B <= 16: the cooperative small-batch kernel
+        return N.net_plan(d, int(batch), 1, int(self.cfg.net_cluster)) is not None
 
     def recommended_use_cuda_graph(self, batch: int | None = None, *, default: bool = False) -> bool:
         """Graph replay pays off whenever the step is launch-bound; the net path is one launch already."""
@@ -341,6 +345,13 @@ class TileLangIPC:
                 desc.e[l] = self.e[l].data_ptr()
             for l in range(self.L + 1):
                 desc.x[l] = self.x[l].data_ptr()
+            plan = N.net_plan(self.cfg.dims, desc.B, 1, int(self.cfg.net_cluster))
+            if plan is not None and plan[0] == 0:
+                # the wide small-batch kernel: activation cache a[l] = cast(f(x[l])) written where x is
+                # produced, so every CTA stages f(x) without recomputing it
+                self._net_acache = [None] + [torch.empty_like(self.x[l]) for l in range(1, self.L + 1)]
+                for l in range(1, self.L + 1):
+                    desc.a[l] = self._net_acache[l].data_ptr()
             self._net_desc = desc
         return self._net_desc
 
@@ -363,6 +374,9 @@ class TileLangIPC:
         run.alpha, run.gamma = float(self.cfg.alpha), float(self.cfg.gamma)
         run.act, run.dtype = self.act.code, N.dtype_code(self.cfg.dtype)
         run.cluster = int(self.cfg.net_cluster)
+        if self._net_sync is None:  # grid-barrier words of the wide small-batch kernel (zeroed per launch)
+            self._net_sync = torch.zeros(N.NET_SYNC_BYTES // 4, device=self.device, dtype=torch.int32)
+        run.sync = self._net_sync.data_ptr()
         N.check(N.load().ipc_net_train(self._net(), run, N.stream_handle(self.device)))
 
     # ----------------------------------------------------------------- steps
