@@ -14,13 +14,14 @@
 //           I: x[l] += g(-e[l] + f'(x[l]) W[l-1]^T e[l-1]) for l >= 1 (one phase)
 //   W       W[l] = cast(W[l] + a e[l] f(x[l+1])^T) for all l          (one phase)
 // A GEMM phase is a list of units (layer, 32 output rows).  A CTA stages the
-// unit's thin operand (f applied, K x B) in shared memory, transposed for the
-// col-major mma operand; its 16 warps cover 2 row tiles x 8 K slices, load
-// their W fragments straight from L2 (ld.global.cg: W and the states change
-// between phases, and L1 is not coherent across SMs) and run mma.sync
-// m16n8k16; the 8 K-slice partials are summed in shared memory in fixed order
-// and the fused epilogue of the phase stores the result.  The weight phase is
-// an outer product on the CUDA cores (B <= 16 terms per element).
+// unit's thin operand (K x B, f applied or read from the activation cache) in
+// shared memory as rows of 16 batch columns; its 16 warps cover 2 row tiles x 8
+// K slices, load their W fragments straight from L2 (ld.global.cg: W and the
+// states change between phases, and L1 is not coherent across SMs), take the
+// B fragments with ldmatrix.trans and run mma.sync m16n8k16; the 8 K-slice
+// partials are summed in shared memory in fixed order and the fused epilogue
+// of the phase stores the result.  The weight phase runs dW tiles as mma.sync
+// with the batch (B <= 16, zero-padded) as the reduction.
 // Rounding points are those of the operator kernels: tilelang_kernels.py:163,
 // 173, 229-230, 320 and the forward sweep trainer.py:513-515.
 //
@@ -48,7 +49,7 @@ constexpr long long WN_WAIT_NS = 2000000000LL;
 
 template <typename T>
 struct WideParams {
-  int L, B, kmax, sld;
+  int L, B, kmax;
   int dims[IPC_NET_MAX_LAYERS + 1];
   T* w[IPC_NET_MAX_LAYERS];
   T* x[IPC_NET_MAX_LAYERS + 1];
@@ -158,17 +159,20 @@ __device__ __forceinline__ uint32_t wn_load_a(const unsigned short* A, int M, in
   }
 }
 
-// Stage a thin operand src [K][B] (row-major, B <= 16) into sX[n][k] for n < B, k < K, with f applied
-// (apply_f) and rounded to the storage type; columns [K, Kz) are zeroed.  The source is read as 16-byte
-// vectors, all of a thread's loads issued before any is used (one L2 round trip for K x B <= 32 K elements).
+// Thin operands live in shared memory as sT[k][16] (the batch columns of row k, zero past B),
+// 32 bytes per row, the two 16-byte halves of a row swapped on every other group of four rows so
+// that ldmatrix reads of 8 consecutive rows hit 8 distinct bank groups.
+__device__ __forceinline__ int wn_swz(int k, int n) { return k * WN_NC + ((((n >> 3) ^ (k >> 2)) & 1) << 3) + (n & 7); }
+
+// Stage src [K][B] (row-major) into sT rows [0, K) with f applied (APPLY_F) and rounded to the
+// storage type, and zero rows [K, Kz).  Columns n >= B are zeroed once per launch and never
+// written.  B = 16 rows are 16-byte vector copies; other widths go element by element.
 template <typename T, int ACT, bool APPLY_F>
-__device__ __forceinline__ void wn_stage(const T* __restrict__ src, int K, int B, int Kz, int sld, T* sX) {
-  constexpr int NV = 2;  // 16-byte vectors per thread per round
+__device__ __forceinline__ void wn_stage(const T* __restrict__ src, int K, int B, int Kz, T* sT) {
+  constexpr int NV = 2;  // 16-byte vectors per thread per round, all loaded before any is stored
   const int tid = threadIdx.x;
-  const int n_el = K * B;
-  int done = 0;
-  if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-    const int nvec = n_el >> 3;
+  if (B == WN_NC && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    const int nvec = 2 * K;  // two halves per row
     const uint4* sv = reinterpret_cast<const uint4*>(src);
     for (int base = tid; base < nvec; base += WN_THREADS * NV) {
       uint4 v[NV];
@@ -181,37 +185,44 @@ __device__ __forceinline__ void wn_stage(const T* __restrict__ src, int K, int B
       for (int j = 0; j < NV; ++j) {
         const int c = base + j * WN_THREADS;
         if (c >= nvec) break;
-        const T* h = reinterpret_cast<const T*>(&v[j]);
+        if constexpr (APPLY_F) {
+          T* h = reinterpret_cast<T*>(&v[j]);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int idx = 8 * c + q;
-          const int k = idx / B, n = idx - k * B;
-          float f = St<T>::ld(h[q]);
-          if constexpr (APPLY_F) f = rnd<T>(act_f<ACT>(f));
-          sX[n * sld + k] = St<T>::st(f);
+          for (int q = 0; q < 8; ++q) h[q] = St<T>::st(act_f<ACT>(St<T>::ld(h[q])));
         }
+        const int k = c >> 1;
+        *reinterpret_cast<uint4*>(sT + wn_swz(k, (c & 1) * 8)) = v[j];
       }
     }
-    done = nvec << 3;
+  } else {
+    for (int idx = tid; idx < K * B; idx += WN_THREADS) {
+      const int k = idx / B, n = idx - k * B;
+      float f = ldcg(src + idx);
+      if constexpr (APPLY_F) f = act_f<ACT>(f);
+      sT[wn_swz(k, n)] = St<T>::st(f);
+    }
   }
-  for (int idx = done + tid; idx < n_el; idx += WN_THREADS) {
-    const int k = idx / B, n = idx - k * B;
-    float f = ldcg(src + idx);
-    if constexpr (APPLY_F) f = rnd<T>(act_f<ACT>(f));
-    sX[n * sld + k] = St<T>::st(f);
-  }
-  for (int i = tid; i < (Kz - K) * B; i += WN_THREADS) sX[(i % B) * sld + K + i / B] = St<T>::st(0.f);
+  for (int i = tid; i < (Kz - K) * WN_NC; i += WN_THREADS) sT[K * WN_NC + i] = St<T>::st(0.f);
+}
+
+__device__ __forceinline__ void wn_ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
 }
 
 // One GEMM phase over layers [l0, l1].  energy != nullptr: add sum_l mean(e[l]^2) (P only).
 // PAIRS (I only, every hidden width even): W_low fragments from 32-bit loads of row pairs.
 template <typename T, int ACT, int MODE, bool PAIRS, bool ACC>
-__device__ void wn_gemm_phase(const WideParams<T>& p, int l0, int l1, float* energy, float* red, T* sX) {
+__device__ void wn_gemm_phase(const WideParams<T>& p, int l0, int l1, float* energy, float* red, T* sT) {
   constexpr int KSTEPS = 8;  // k16 steps whose W fragments a warp loads before using any
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gq = lane >> 2, tq = lane & 3;
   const int tile = warp & 1, ksl = warp >> 1;
-  const int B = p.B, sld = p.sld;
+  const int B = p.B;
+  // ldmatrix.x4.trans row address of this lane: matrix (lane >> 3) = (k half, n half), row lane & 7
+  const int lm_k = (lane & 7) + ((lane >> 3) & 1) * 8, lm_n = (lane >> 4) * 8;
   int total = 0;
   for (int l = l0; l <= l1; ++l) total += (p.dims[l] + WN_ROWS - 1) / WN_ROWS;
   for (int u = blockIdx.x; u < total; u += gridDim.x) {
@@ -281,20 +292,18 @@ __device__ void wn_gemm_phase(const WideParams<T>& p, int l0, int l1, float* ene
         }
       }
       if (!staged) {
-        wn_stage<T, ACT, (MODE != WN_I) && !from_cache>(src, K, B, Kp, sld, sX);
+        wn_stage<T, ACT, (MODE != WN_I) && !from_cache>(src, K, B, Kp, sT);
         __syncthreads();
         staged = true;
       }
 #pragma unroll
       for (int st = 0; st < KSTEPS; ++st) {
         if (kb + 16 * st >= kb1) break;
-        const int kl = kb + 16 * st + 2 * tq;
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const T* col = sX + (8 * j + gq) * sld + kl;
-          wn_mma<T>(acc[j], a[st], *reinterpret_cast<const uint32_t*>(col),
-                    *reinterpret_cast<const uint32_t*>(col + 8));
-        }
+        uint32_t b[4];  // b0, b1 of n-tile 0, then of n-tile 1
+        const int k = kb + 16 * st + lm_k;
+        wn_ldmatrix_x4_trans(b, sT + wn_swz(k, lm_n));
+        wn_mma<T>(acc[0], a[st], b[0], b[1]);
+        wn_mma<T>(acc[1], a[st], b[2], b[3]);
       }
     }
     // partials by physical row of the tile
@@ -333,16 +342,20 @@ __device__ void wn_gemm_phase(const WideParams<T>& p, int l0, int l1, float* ene
       for (int o = 16; o > 0; o >>= 1) esum += __shfl_xor_sync(0xffffffffu, esum, o);
       if (lane == 0 && esum != 0.f) atomicAdd(energy, esum);
     }
-    __syncthreads();  // sX / red are rewritten by the next unit
+    __syncthreads();  // sT / red are rewritten by the next unit
   }
 }
 
-// W[l] = cast(W[l] + alpha e[l] f(x[l+1])^T) for every layer (outer product over B <= 16 columns).
+// W[l] = cast(W[l] + alpha e[l] f(x[l+1])^T) for every layer.  dW of a 16 x 8 tile is one
+// mma.sync m16n8k16 with the batch (B <= 16, zero-padded) as the reduction: A = the unit's rows of
+// e[l] (sE[32][16]), B(n, c) = f(x[l+1])[c][n] straight from the staged rows of sT.
 template <typename T, int ACT, bool ACC>
-__device__ void wn_weight_phase(const WideParams<T>& p, float* sE, T* sX) {
-  constexpr int NI = 4;  // W vectors a thread loads before updating any
-  const int tid = threadIdx.x;
-  const int B = p.B, sld = p.sld;
+__device__ void wn_weight_phase(const WideParams<T>& p, T* sE, T* sT) {
+  constexpr int NT = 8;  // n-tiles whose W values a warp loads before updating any
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int mt = warp & 1, wq = warp >> 1;  // m-tile, and this warp's share of the n-tiles
+  const int B = p.B;
   int total = 0;
   for (int l = 0; l < p.L; ++l) total += (p.dims[l] + WN_ROWS - 1) / WN_ROWS;
   for (int u = blockIdx.x; u < total; u += gridDim.x) {
@@ -357,46 +370,62 @@ __device__ void wn_weight_phase(const WideParams<T>& p, float* sE, T* sX) {
     for (int i = tid; i < WN_ROWS * WN_NC; i += WN_THREADS) {
       const int rr = i / WN_NC, n = i % WN_NC;
       const int m = row0 + rr;
-      sE[i] = (m < M && n < B) ? ldcg(p.e[l] + (long long)m * B + n) : 0.f;
+      sE[i] = St<T>::st((m < M && n < B) ? ldcg(p.e[l] + m * B + n) : 0.f);
     }
-    wn_stage<T, ACT, !ACC>(ACC ? p.a[l + 1] : p.x[l + 1], K, B, K8, sld, sX);
+    wn_stage<T, ACT, !ACC>(ACC ? p.a[l + 1] : p.x[l + 1], K, B, K8, sT);
     __syncthreads();
-    const int nk8 = K8 / 8;
-    const int items = min(WN_ROWS, M - row0) * nk8;
+    uint32_t a[4];
+    {
+      const T* e0 = sE + (mt * 16 + gq) * WN_NC + 2 * tq;
+      a[0] = *reinterpret_cast<const uint32_t*>(e0);
+      a[1] = *reinterpret_cast<const uint32_t*>(e0 + 8 * WN_NC);
+      a[2] = *reinterpret_cast<const uint32_t*>(e0 + 8);
+      a[3] = *reinterpret_cast<const uint32_t*>(e0 + 8 * WN_NC + 8);
+    }
+    const int m0 = row0 + mt * 16 + gq, m1 = m0 + 8;
+    const bool even = (K % 2) == 0;
     T* W = p.w[l];
-    const bool vec = (K % 8) == 0;
-    for (int base = tid; base < items; base += WN_THREADS * NI) {
-      uint4 wv[NI];
-      if (vec) {
+    const int ntiles = K8 / 8;
+    for (int j0 = wq; j0 < ntiles; j0 += WN_KSLICES * NT) {
+      uint32_t w0[NT], w1[NT];
 #pragma unroll
-        for (int j = 0; j < NI; ++j) {
-          const int i = base + j * WN_THREADS;
-          if (i < items) wv[j] = __ldcg(reinterpret_cast<const uint4*>(W + (long long)(row0 + i / nk8) * K + (i % nk8) * 8));
+      for (int q = 0; q < NT; ++q) {
+        const int c = (j0 + q * WN_KSLICES) * 8 + 2 * tq;
+        w0[q] = w1[q] = 0u;
+        if (even && c < K) {
+          if (m0 < M) w0[q] = __ldcg(reinterpret_cast<const uint32_t*>(W + m0 * K + c));
+          if (m1 < M) w1[q] = __ldcg(reinterpret_cast<const uint32_t*>(W + m1 * K + c));
         }
       }
 #pragma unroll
-      for (int j = 0; j < NI; ++j) {
-        const int i = base + j * WN_THREADS;
-        if (i >= items) break;
-        const int rr = i / nk8, k8 = (i % nk8) * 8;
-        float acc[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = 0.f;
-        for (int n = 0; n < B; ++n) {
-          const float ev = sE[rr * WN_NC + n];
-          const uint4 raw = *reinterpret_cast<const uint4*>(sX + n * sld + k8);
-          const T* h = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) acc[q] = fmaf(ev, St<T>::ld(h[q]), acc[q]);
-        }
-        T* wr = W + (long long)(row0 + rr) * K + k8;
-        if (vec) {
-          T* wh = reinterpret_cast<T*>(&wv[j]);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) wh[q] = St<T>::st(St<T>::ld(wh[q]) + p.alpha * acc[q]);
-          *reinterpret_cast<uint4*>(wr) = wv[j];
+      for (int q = 0; q < NT; ++q) {
+        const int j = j0 + q * WN_KSLICES;
+        if (j >= ntiles) break;
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(sT + wn_swz(j * 8 + gq, 2 * tq));
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(sT + wn_swz(j * 8 + gq, 2 * tq + 8));
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        wn_mma<T>(d, a, b0, b1);
+        const int c = j * 8 + 2 * tq;
+        if (even) {
+          if (c < K && m0 < M) {
+            T* h = reinterpret_cast<T*>(&w0[q]);
+            h[0] = St<T>::st(St<T>::ld(h[0]) + p.alpha * d[0]);
+            h[1] = St<T>::st(St<T>::ld(h[1]) + p.alpha * d[1]);
+            *reinterpret_cast<uint32_t*>(W + m0 * K + c) = w0[q];
+          }
+          if (c < K && m1 < M) {
+            T* h = reinterpret_cast<T*>(&w1[q]);
+            h[0] = St<T>::st(St<T>::ld(h[0]) + p.alpha * d[2]);
+            h[1] = St<T>::st(St<T>::ld(h[1]) + p.alpha * d[3]);
+            *reinterpret_cast<uint32_t*>(W + m1 * K + c) = w1[q];
+          }
         } else {
-          for (int q = 0; q < 8 && k8 + q < K; ++q) wr[q] = St<T>::st(ldcg(wr + q) + p.alpha * acc[q]);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (c + h >= K) continue;
+            if (m0 < M) W[m0 * K + c + h] = St<T>::st(ldcg(W + m0 * K + c + h) + p.alpha * d[h]);
+            if (m1 < M) W[m1 * K + c + h] = St<T>::st(ldcg(W + m1 * K + c + h) + p.alpha * d[2 + h]);
+          }
         }
       }
     }
@@ -407,11 +436,14 @@ __device__ void wn_weight_phase(const WideParams<T>& p, float* sE, T* sX) {
 template <typename T, int ACT, bool PAIRS, bool ACC>
 __global__ void __launch_bounds__(WN_THREADS, 1) wide_net_kernel(const __grid_constant__ WideParams<T> p) {
   extern __shared__ __align__(16) uint8_t wn_smem[];
-  float* red = reinterpret_cast<float*>(wn_smem);  // [16 warps][16][16]
-  float* sE = red + WN_WARPS * 16 * WN_NC;         // [32][16]
-  T* sX = reinterpret_cast<T*>(sE + WN_ROWS * WN_NC);
+  float* red = reinterpret_cast<float*>(wn_smem);                 // [16 warps][16][16] fp32
+  T* sE = reinterpret_cast<T*>(red + WN_WARPS * 16 * WN_NC);      // [32][16]
+  T* sT = sE + WN_ROWS * WN_NC;                                   // [kmax][16], swizzled halves
   const int L = p.L, B = p.B;
   unsigned epoch = 0;  // grid barriers passed in this launch
+  if (B < WN_NC)  // batch columns past B stay zero for the whole launch (staging never writes them)
+    for (int i = threadIdx.x; i < p.kmax * WN_NC; i += WN_THREADS) sT[i] = St<T>::st(0.f);
+  __syncthreads();
   for (int step = 0; step < p.steps; ++step) {
     long long* tr = (p.phase_ns != nullptr && step < IPC_NET_TRACE_STEPS && blockIdx.x == 0 && threadIdx.x == 0)
                         ? p.phase_ns + (long long)step * IPC_NET_TRACE_PHASES
@@ -445,25 +477,25 @@ __global__ void __launch_bounds__(WN_THREADS, 1) wide_net_kernel(const __grid_co
     if (tr) tr[WT_BATCH] = wn_now();
     if (p.forward_init) {
       for (int l = L - 1; l >= 1; --l) {
-        wn_gemm_phase<T, ACT, WN_F, false, ACC>(p, l, l, nullptr, red, sX);
+        wn_gemm_phase<T, ACT, WN_F, false, ACC>(p, l, l, nullptr, red, sT);
         if (!wn_grid_sync(p.sync, epoch)) return;
       }
     }
     if (tr) tr[WT_FORWARD] = wn_now();
     for (int t = 0; t < p.T_it; ++t) {
       float* en = (t == p.T_it - 1 && p.energy != nullptr) ? p.energy + step : nullptr;
-      wn_gemm_phase<T, ACT, WN_P, false, ACC>(p, 0, L - 1, en, red, sX);
+      wn_gemm_phase<T, ACT, WN_P, false, ACC>(p, 0, L - 1, en, red, sT);
       if (!wn_grid_sync(p.sync, epoch)) return;
       if (tr && t == 0) tr[WT_P0] = wn_now();
       if (L > 1) {
-        wn_gemm_phase<T, ACT, WN_I, PAIRS, ACC>(p, 1, L - 1, nullptr, red, sX);
+        wn_gemm_phase<T, ACT, WN_I, PAIRS, ACC>(p, 1, L - 1, nullptr, red, sT);
         if (!wn_grid_sync(p.sync, epoch)) return;
       }
       if (tr && t == 0) tr[WT_I0] = wn_now();
     }
     if (tr) tr[WT_ITER] = wn_now();
     if (p.update_weights) {
-      wn_weight_phase<T, ACT, ACC>(p, sE, sX);
+      wn_weight_phase<T, ACT, ACC>(p, sE, sT);
       if (!wn_grid_sync(p.sync, epoch)) return;
     }
     if (tr) tr[WT_W] = wn_now();
@@ -498,7 +530,6 @@ int wn_prepare(WideParams<T>& p, const ipc_net_t* net, const ipc_net_run_t* run,
   if (!p.acache)
     for (int l = 0; l <= net->L; ++l) p.a[l] = nullptr;
   p.kmax = (kmax + 63) & ~63;
-  p.sld = p.kmax + 8;  // 4 words mod 32 per row: conflict-free fragment reads
   if (run != nullptr) {
     p.pool_x = reinterpret_cast<const T*>(run->pool_x);
     p.pool_y = reinterpret_cast<const T*>(run->pool_y);
@@ -514,8 +545,8 @@ int wn_prepare(WideParams<T>& p, const ipc_net_t* net, const ipc_net_run_t* run,
     p.sync = reinterpret_cast<unsigned*>(run->sync);
     p.phase_ns = run->phase_ns;
   }
-  *smem = (size_t)WN_WARPS * 16 * WN_NC * sizeof(float) + (size_t)WN_ROWS * WN_NC * sizeof(float) +
-          (size_t)WN_NC * p.sld * sizeof(T);
+  *smem = (size_t)WN_WARPS * 16 * WN_NC * sizeof(float) + (size_t)WN_ROWS * WN_NC * sizeof(T) +
+          (size_t)p.kmax * WN_NC * sizeof(T);
   return IPC_OK;
 }
 
