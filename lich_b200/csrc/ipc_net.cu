@@ -9,7 +9,7 @@
 // the cost that dominates at hidden 64 -- is paid once per launch, and the
 // network state never leaves the chip between steps.
 //
-// Decomposition.  Network n runs on a cluster of C CTAs (C <= 8).
+// Decomposition.  Network n runs on a cluster of C CTAs (C <= 8, or 16 on request).
 //  * Batch columns: CTA c owns columns [c*NCOL, (c+1)*NCOL) of every state.
 //    Prediction errors and state updates are column-local, so the T inference
 //    iterations need only __syncthreads.
@@ -59,7 +59,8 @@ constexpr int NET_THREADS = 512;
 constexpr int NET_WARPS = NET_THREADS / 32;
 constexpr int WLD = 72;  // smem row stride (elements) of replicated hidden W tiles (<= 64 cols + 8)
 constexpr int MAXL = IPC_NET_MAX_LAYERS;
-constexpr int MAX_CLUSTER = 8;
+constexpr int MAX_CLUSTER = 16;           // above 8 CTAs the cluster is non-portable (opt-in attribute)
+constexpr int MAX_PORTABLE_CLUSTER = 8;
 constexpr int MAX_OWN = MAXL;  // hidden layers owned per CTA
 constexpr int SMEM_LIMIT = 227 * 1024;
 
@@ -333,11 +334,19 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
           frag_b_kn(bf, sbase + p.o_al, p.ald, ks * 16, nt * 8, lane);
           mma<T>(acc, af, bf[0], bf[1]);
         }
-        const int r = mt * 16 + gq, n = nt * 8 + 2 * tq;
+        // lanes tq, tq ^ 1 swap halves so each sends four consecutive columns of one row in a
+        // single 16-byte store: even tq row gq, odd tq row gq + 8
+        const bool odd = tq & 1;
+        const float s0 = odd ? acc[0] : acc[2], s1 = odd ? acc[1] : acc[3];
+        const float o0 = __shfl_xor_sync(0xffffffffu, s0, 1), o1 = __shfl_xor_sync(0xffffffffu, s1, 1);
+        const int r = mt * 16 + gq + (odd ? 8 : 0), n = nt * 8 + 2 * (tq & ~1);
         const int owner = n / NCOL, lc = n % NCOL;
         const uint32_t dst = mapa(recv_base + 4 * ((cta * p.rows16[Lt] + r) * NCOL + lc), owner);
-        st_dsmem_f2(dst, acc[0], acc[1]);
-        st_dsmem_f2(dst + 4 * 8 * NCOL, acc[2], acc[3]);
+        const uint4 v = odd ? make_uint4(__float_as_uint(o0), __float_as_uint(o1), __float_as_uint(acc[2]),
+                                         __float_as_uint(acc[3]))
+                            : make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(o0),
+                                         __float_as_uint(o1));
+        st_dsmem_v4(dst, v);
       }
     }
     trace(step, 1);
@@ -565,20 +574,49 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
             mma<T>(acc, af, bf[0], bf[1]);
           }
           const int n = nt * 8 + 2 * tq;
+          if (cols % 8 == 0) {
+            // whole 8-column segments: the 4 lanes of a row gather their pairs so one lane per row
+            // pushes the segment to every replica as a single 16-byte store
+            uint32_t v[2] = {0u, 0u};
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
+            for (int h = 0; h < 2; ++h) {
+              const int rr = mt * 16 + gq + 8 * h;
+              if (rr < p.dims[l] && n < cols) {
+                float w0, w1;
+                unpack2<T>(U32(p.o_w[l], rr * WLD + n), w0, w1);
+                v[h] = bits2<T>(w0 + p.alpha * acc[2 * h], w1 + p.alpha * acc[2 * h + 1]);
+              }
+            }
+            uint32_t seg[4];
+            const int h = tq & 1;  // tq 0 pushes row gq, tq 1 row gq + 8
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t a0 = __shfl_sync(0xffffffffu, v[0], gq * 4 + j);
+              const uint32_t a1 = __shfl_sync(0xffffffffu, v[1], gq * 4 + j);
+              seg[j] = h ? a1 : a0;
+            }
             const int rr = mt * 16 + gq + 8 * h;
-            if (rr >= p.dims[l] || n >= cols) continue;
-            const int idx = rr * WLD + n;
-            const uint32_t a = sbase + p.o_w[l] + 2 * idx;
-            if (n + 1 < cols) {
-              float w0, w1;
-              unpack2<T>(U32(p.o_w[l], idx), w0, w1);
-              const uint32_t v = bits2<T>(w0 + p.alpha * acc[2 * h], w1 + p.alpha * acc[2 * h + 1]);
-              for (int cc = 0; cc < C; ++cc) st_dsmem_u32(mapa(a, cc), v);
-            } else {
-              const uint16_t v = bits<T>(St<T>::ld(S(p.o_w[l])[idx]) + p.alpha * acc[2 * h]);
-              for (int cc = 0; cc < C; ++cc) st_dsmem_u16(mapa(a, cc), v);
+            if (tq < 2 && rr < p.dims[l] && nt * 8 < cols) {
+              const uint32_t a = sbase + p.o_w[l] + 2 * (rr * WLD + nt * 8);
+              const uint4 sv = make_uint4(seg[0], seg[1], seg[2], seg[3]);
+              for (int cc = 0; cc < C; ++cc) st_dsmem_v4(mapa(a, cc), sv);
+            }
+          } else {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int rr = mt * 16 + gq + 8 * h;
+              if (rr >= p.dims[l] || n >= cols) continue;
+              const int idx = rr * WLD + n;
+              const uint32_t a = sbase + p.o_w[l] + 2 * idx;
+              if (n + 1 < cols) {
+                float w0, w1;
+                unpack2<T>(U32(p.o_w[l], idx), w0, w1);
+                const uint32_t v = bits2<T>(w0 + p.alpha * acc[2 * h], w1 + p.alpha * acc[2 * h + 1]);
+                for (int cc = 0; cc < C; ++cc) st_dsmem_u32(mapa(a, cc), v);
+              } else {
+                const uint16_t v = bits<T>(St<T>::ld(S(p.o_w[l])[idx]) + p.alpha * acc[2 * h]);
+                for (int cc = 0; cc < C; ++cc) st_dsmem_u16(mapa(a, cc), v);
+              }
             }
           }
         }
@@ -676,8 +714,9 @@ int make_layout(NetParams<T>& p, int C, int NCOL) {
   return off;
 }
 
-// Pick columns per CTA (prefer 16, then 8, then 32) with a cluster of <= 8 CTAs
-// whose layout fits in shared memory; `want` > 0 forces the cluster size.
+// Pick columns per CTA (prefer 16, then 8, then 32) with a portable cluster of <= 8 CTAs
+// whose layout fits in shared memory; `want` > 0 forces the cluster size, up to 16 (a
+// non-portable cluster: one network over twice the SMs).
 template <typename T>
 int choose_plan(NetParams<T>& p, int want, int* ncol_out) {
   const int pref[3] = {16, 8, 32};
@@ -685,14 +724,15 @@ int choose_plan(NetParams<T>& p, int want, int* ncol_out) {
     const int ncol = pref[i];
     if (p.B % ncol != 0) continue;
     const int C = p.B / ncol;
-    if (C > MAX_CLUSTER || (want > 0 && C != want)) continue;
+    if (C > (want > 0 ? MAX_CLUSTER : MAX_PORTABLE_CLUSTER) || (want > 0 && C != want)) continue;
     if (make_layout(p, C, ncol) <= SMEM_LIMIT) {
       *ncol_out = ncol;
       return IPC_OK;
     }
   }
   return set_error(IPC_ERR_UNSUPPORTED,
-                   "net kernel: no cluster of <= 8 CTAs with 8/16/32 columns each fits B=%d%s in shared memory", p.B,
+                   "net kernel: no cluster of <= 8 (16 on request) CTAs with 8/16/32 columns each fits B=%d%s in "
+                   "shared memory", p.B,
                    want > 0 ? " with the requested cluster size" : "");
 }
 
@@ -700,6 +740,8 @@ template <typename T, int ACT, int NCOL>
 int launch_net_t(NetParams<T>& p, cudaStream_t s) {
   auto kern = net_kernel_act<T, ACT, NCOL>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem_bytes);
+  if (err == cudaSuccess && p.C > MAX_PORTABLE_CLUSTER)
+    err = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "net kernel smem attribute: %s", cudaGetErrorString(err));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.C, p.nets, 1);
