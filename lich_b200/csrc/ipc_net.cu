@@ -168,6 +168,69 @@ __device__ __forceinline__ void unpack2(uint32_t v, float& a, float& b) {
   b = St<T>::ld(*reinterpret_cast<const T*>(&hi));
 }
 
+// ---- two storage values packed in one 32-bit register ----------------------
+// Elementwise work on stored 16-bit states runs on pairs: one cvt packs two
+// fp32 results, the error x - cast(acc) is one hsub2 (a single rounding of the
+// exact difference; the fp32 form rounds the fp32 difference, which is the
+// same value unless the operands are more than 2^13 apart), and f of a stored
+// value is one MUFU op for two elements (tanh.approx.{f16x2,bf16x2}; sigmoid
+// as 0.5 + 0.5 tanh(x / 2); relu as a packed max).
+template <typename T>
+struct Pk;
+template <>
+struct Pk<__half> {
+  using V2 = __half2;
+  static __device__ __forceinline__ V2 as(uint32_t v) { return *reinterpret_cast<const V2*>(&v); }
+  static __device__ __forceinline__ uint32_t bits(V2 v) { return *reinterpret_cast<const uint32_t*>(&v); }
+  static __device__ __forceinline__ uint32_t pack(float a, float b) { return bits(__floats2half2_rn(a, b)); }
+  static __device__ __forceinline__ float2 unpack(uint32_t v) { return __half22float2(as(v)); }
+  static __device__ __forceinline__ uint32_t sub(uint32_t x, uint32_t y) { return bits(__hsub2(as(x), as(y))); }
+  static __device__ __forceinline__ uint32_t fma(uint32_t a, uint32_t b, uint32_t c) {
+    return bits(__hfma2(as(a), as(b), as(c)));
+  }
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) { return bits(__hmul2(as(a), as(b))); }
+  static __device__ __forceinline__ uint32_t max(uint32_t a, uint32_t b) { return bits(__hmax2(as(a), as(b))); }
+  static __device__ __forceinline__ uint32_t splat(float v) { return bits(__float2half2_rn(v)); }
+  static __device__ __forceinline__ uint32_t tanh(uint32_t x) {
+    uint32_t r;
+    asm("tanh.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
+    return r;
+  }
+};
+template <>
+struct Pk<__nv_bfloat16> {
+  using V2 = __nv_bfloat162;
+  static __device__ __forceinline__ V2 as(uint32_t v) { return *reinterpret_cast<const V2*>(&v); }
+  static __device__ __forceinline__ uint32_t bits(V2 v) { return *reinterpret_cast<const uint32_t*>(&v); }
+  static __device__ __forceinline__ uint32_t pack(float a, float b) { return bits(__floats2bfloat162_rn(a, b)); }
+  static __device__ __forceinline__ float2 unpack(uint32_t v) { return __bfloat1622float2(as(v)); }
+  static __device__ __forceinline__ uint32_t sub(uint32_t x, uint32_t y) { return bits(__hsub2(as(x), as(y))); }
+  static __device__ __forceinline__ uint32_t fma(uint32_t a, uint32_t b, uint32_t c) {
+    return bits(__hfma2(as(a), as(b), as(c)));
+  }
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) { return bits(__hmul2(as(a), as(b))); }
+  static __device__ __forceinline__ uint32_t max(uint32_t a, uint32_t b) { return bits(__hmax2(as(a), as(b))); }
+  static __device__ __forceinline__ uint32_t splat(float v) { return bits(__float2bfloat162_rn(v)); }
+  static __device__ __forceinline__ uint32_t tanh(uint32_t x) {
+    uint32_t r;
+    asm("tanh.approx.bf16x2 %0, %1;" : "=r"(r) : "r"(x));
+    return r;
+  }
+};
+
+// f of a stored pair, packed where the activation has a packed form (else per element)
+template <typename T, int ACT>
+__device__ __forceinline__ uint32_t act_pair(uint32_t x) {
+  if constexpr (ACT == IPC_ACT_RELU) {
+    return Pk<T>::max(x, 0u);
+  } else if constexpr (ACT == IPC_ACT_IDENTITY) {
+    return x;
+  } else {
+    const float2 v = Pk<T>::unpack(x);
+    return Pk<T>::pack(act_f_hw<ACT>(v.x), act_f_hw<ACT>(v.y));
+  }
+}
+
 // Element offset of (row r, column c) in a swizzled [rows][NCOL] state tile:
 // 16-byte chunk j of row r is stored at chunk j ^ s(r).
 template <int NCOL>
@@ -275,18 +338,14 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
     for (int it = threadIdx.x; it < kcnt * (B / 2); it += NET_THREADS) {
       const int r = it / (B / 2), c = (it % (B / 2)) * 2;
       uint32_t& v = U32(p.o_al, r * p.ald + c);
-      float a, b;
-      unpack2<T>(v, a, b);
-      v = bits2<T>(act_f_hw<ACT>(a), act_f_hw<ACT>(b));
+      v = act_pair<T, ACT>(v);
     }
   };
   // a[l] = cast(f(x[l])) over the valid rows of the CTA's columns
   auto act_rows = [&](int l) {
     for (int it = threadIdx.x; it < p.dims[l] * (NCOL / 2); it += NET_THREADS) {
       const int r = it / (NCOL / 2), c = (it % (NCOL / 2)) * 2;
-      float a, b;
-      unpack2<T>(U32(p.o_x[l], sw<NCOL>(r, c)), a, b);
-      U32(p.o_a[l], sw<NCOL>(r, c)) = bits2<T>(act_f_hw<ACT>(a), act_f_hw<ACT>(b));
+      U32(p.o_a[l], sw<NCOL>(r, c)) = act_pair<T, ACT>(U32(p.o_x[l], sw<NCOL>(r, c)));
     }
   };
 
@@ -373,10 +432,8 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
         for (int it = threadIdx.x; it < dT * (NCOL / 2); it += NET_THREADS) {
           const int r = it / (NCOL / 2), c = (it % (NCOL / 2)) * 2;
           const uint32_t v = U32(p.o_mu, sw<NCOL>(r, c));
-          float a, b;
-          unpack2<T>(v, a, b);
           U32(p.o_x[Lt], sw<NCOL>(r, c)) = v;
-          U32(p.o_a[Lt], sw<NCOL>(r, c)) = bits2<T>(act_f_hw<ACT>(a), act_f_hw<ACT>(b));
+          U32(p.o_a[Lt], sw<NCOL>(r, c)) = act_pair<T, ACT>(v);
         }
         __syncthreads();
       }
@@ -396,9 +453,9 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
           for (int h = 0; h < 2; ++h) {
             const int rr = mt * 16 + gq + 8 * h;
             if (rr >= p.dims[l]) continue;
-            U32(p.o_x[l], sw<NCOL>(rr, c)) = bits2<T>(acc[2 * h], acc[2 * h + 1]);
-            U32(p.o_a[l], sw<NCOL>(rr, c)) =
-                bits2<T>(act_f_hw<ACT>(rnd<T>(acc[2 * h])), act_f_hw<ACT>(rnd<T>(acc[2 * h + 1])));
+            const uint32_t xs = Pk<T>::pack(acc[2 * h], acc[2 * h + 1]);
+            U32(p.o_x[l], sw<NCOL>(rr, c)) = xs;
+            U32(p.o_a[l], sw<NCOL>(rr, c)) = act_pair<T, ACT>(xs);
           }
         }
         __syncthreads();
@@ -428,9 +485,7 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
               const int rr = mt * 16 + gq + 8 * h;
               if (rr >= p.dims[l]) continue;
               const int i = sw<NCOL>(rr, c);
-              float xa, xb;
-              unpack2<T>(U32(p.o_x[l], i), xa, xb);
-              U32(p.o_e[l], i) = bits2<T>(xa - rnd<T>(acc[2 * h]), xb - rnd<T>(acc[2 * h + 1]));
+              U32(p.o_e[l], i) = Pk<T>::sub(U32(p.o_x[l], i), Pk<T>::pack(acc[2 * h], acc[2 * h + 1]));
             }
           }
           base += units;
@@ -438,10 +493,7 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
         for (int it = threadIdx.x; it < dT * (NCOL / 2); it += NET_THREADS) {
           const int r = it / (NCOL / 2), c = (it % (NCOL / 2)) * 2;
           const int i = sw<NCOL>(r, c);
-          float xa, xb, ma, mb;
-          unpack2<T>(U32(p.o_x[Lt], i), xa, xb);
-          unpack2<T>(U32(p.o_mu, i), ma, mb);
-          U32(p.o_e[Lt], i) = bits2<T>(xa - ma, xb - mb);
+          U32(p.o_e[Lt], i) = Pk<T>::sub(U32(p.o_x[Lt], i), U32(p.o_mu, i));
         }
       }
       __syncthreads();
@@ -465,13 +517,12 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
               const int rr = mt * 16 + gq + 8 * h;
               if (rr >= p.dims[l]) continue;
               const int i = sw<NCOL>(rr, c);
-              float xv[2], ev[2], xn[2];
-              unpack2<T>(U32(p.o_x[l], i), xv[0], xv[1]);
-              unpack2<T>(U32(p.o_e[l], i), ev[0], ev[1]);
-#pragma unroll
-              for (int j = 0; j < 2; ++j) xn[j] = xv[j] + p.gamma * (-ev[j] + act_df_hw<ACT>(xv[j]) * acc[2 * h + j]);
-              U32(p.o_x[l], i) = bits2<T>(xn[0], xn[1]);
-              U32(p.o_a[l], i) = bits2<T>(act_f_hw<ACT>(rnd<T>(xn[0])), act_f_hw<ACT>(rnd<T>(xn[1])));
+              const float2 xv = Pk<T>::unpack(U32(p.o_x[l], i));
+              const float2 ev = Pk<T>::unpack(U32(p.o_e[l], i));
+              const uint32_t xs = Pk<T>::pack(xv.x + p.gamma * (-ev.x + act_df_hw<ACT>(xv.x) * acc[2 * h]),
+                                              xv.y + p.gamma * (-ev.y + act_df_hw<ACT>(xv.y) * acc[2 * h + 1]));
+              U32(p.o_x[l], i) = xs;
+              U32(p.o_a[l], i) = act_pair<T, ACT>(xs);
             }
           }
           base += units;
@@ -714,17 +765,22 @@ int make_layout(NetParams<T>& p, int C, int NCOL) {
   return off;
 }
 
-// Pick columns per CTA (prefer 16, then 8, then 32) with a portable cluster of <= 8 CTAs
-// whose layout fits in shared memory; `want` > 0 forces the cluster size, up to 16 (a
-// non-portable cluster: one network over twice the SMs).
+// Pick columns per CTA and the cluster size whose layout fits in shared memory.  One network
+// per launch is latency-bound, so it is spread over as many SMs as a cluster can have (8
+// columns per CTA, up to 16 CTAs: a non-portable cluster; 29.8 vs 34.1 us per configs[1]
+// depth-6 step); many networks are throughput-bound and keep portable clusters of <= 8 CTAs
+// with 16 columns each.  `want` > 0 forces the cluster size (up to 16).
 template <typename T>
 int choose_plan(NetParams<T>& p, int want, int* ncol_out) {
-  const int pref[3] = {16, 8, 32};
+  const bool one = p.nets == 1 && want == 0;
+  const int pref_one[3] = {8, 16, 32}, pref_many[3] = {16, 8, 32};
+  const int* pref = one ? pref_one : pref_many;
   for (int i = 0; i < 3; ++i) {
     const int ncol = pref[i];
     if (p.B % ncol != 0) continue;
     const int C = p.B / ncol;
-    if (C > (want > 0 ? MAX_CLUSTER : MAX_PORTABLE_CLUSTER) || (want > 0 && C != want)) continue;
+    const int cmax = (want > 0 || one) ? MAX_CLUSTER : MAX_PORTABLE_CLUSTER;
+    if (C > cmax || (want > 0 && C != want)) continue;
     if (make_layout(p, C, ncol) <= SMEM_LIMIT) {
       *ncol_out = ncol;
       return IPC_OK;
