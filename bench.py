@@ -314,8 +314,8 @@ def run_c2(args, world, rank, local):
 # ncu dram__bytes_read.sum + dram__bytes_write.sum per training step of the persistent
 # kernel, from the captures summarised in profiles/ (filled in after each capture).
 TRAFFIC_PER_STEP: dict = {
-    # profiles/net_kernel_c2_depth6.md: 10,407,424 B read + 0 B written over a 50-step launch
-    ("c2", 6): 10407424 / 50,
+    # profiles/net_kernel_c2_depth6.md: 10,393,856 B read + 0 B written over a 50-step launch
+    ("c2", 6): 10393856 / 50,
 }
 
 
