@@ -930,7 +930,17 @@ def run_reference(args, world, rank):
                     "d2h_bytes_per_step": 0}}
 
 
+def _emit(fd: int, line: dict) -> None:
+    """The result line, alone, on the original standard output."""
+    os.write(fd, (json.dumps(line) + "\n").encode())
+
+
 def main():
+    # Everything printed by libraries (NCCL banners, warnings) goes to stderr; the one JSON line is
+    # written to the original stdout by _emit.
+    sys.stdout.flush()
+    result_fd = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10000)
@@ -955,7 +965,7 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         line = run_reference(args, world, rank)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            _emit(result_fd, line)
         return
     if "--steps" not in sys.argv:
         args.steps = {"c5": 5, "c4b": 200, "c4a": 500}.get(args.config, args.steps)
@@ -965,7 +975,7 @@ def main():
     runners = {"c2": run_c2, "c3": run_c3, "c4a": run_c4a, "c4b": run_c4b, "c5": run_c5}
     line = runners[args.config](args, world, rank, local)
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        _emit(result_fd, line)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
