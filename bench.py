@@ -787,6 +787,35 @@ def run_c4a(args, world, rank, local):
     return line
 
 
+def cpu_c3(M, K, B, budget_s=20.0):
+    """configs[2] on the host: the reference's fp32 torch expressions of P, I and W
+    (``tilelang_kernels.py:159-173, 219-231, 304-320`` as plain tensor ops) on all cores."""
+    from oracle import ipc_oracle as O
+    model, ncpu = cpu_info()
+    torch.set_num_threads(ncpu)
+    g = torch.Generator().manual_seed(3)
+    x_up = torch.randn((K, B), generator=g)
+    w = torch.randn((M, K), generator=g) / K ** 0.5
+    x_lo = torch.randn((M, B), generator=g)
+    w_low = torch.randn((K, M), generator=g) / M ** 0.5
+    e_low = torch.randn((K, B), generator=g)
+    ops = {
+        "P": lambda: x_lo - w @ O.act_forward("tanh", x_up),
+        "I": lambda: x_lo + 0.5 * (-x_lo + O.act_derivative("tanh", x_lo) * (w_low.t() @ e_low)),
+        "W_recompute": lambda: w + 1e-4 * (x_lo @ O.act_forward("tanh", x_up).t()),
+    }
+    out = {}
+    t_all = time.perf_counter()
+    for name, fn in ops.items():
+        fn()
+        t0, n = time.perf_counter(), 0
+        while n < 1 or (time.perf_counter() - t0 < budget_s / 6 and n < 50):
+            fn()
+            n += 1
+        out[name] = (time.perf_counter() - t0) / n
+    return out, ncpu, model, time.perf_counter() - t_all
+
+
 C3_SIZES = (64, 256, 1024, 4096, 8192)
 C3_BATCHES = (128, 1024, 8192, 65536)
 
@@ -802,6 +831,19 @@ def _c3_algo(kind, M, K, B):
     if mg >= 128 and ng >= 128 and kg >= 64 and mg * ng * kg >= 128 * 256 * 256:
         return "tcgen05"
     return "mma.sync"
+
+
+def _c3_cpu_line(M, B, pk):
+    """cpu_baseline of configs[2]: the headline point's kernel (P) on the host, in the same metric
+    (fraction of the measured B200 peak that the host's time corresponds to)."""
+    times, ncpu, model, _ = cpu_c3(M, M, B)
+    flop = 2.0 * M * M * B
+    nbytes = (M * M + M * B + 2 * M * B) * 2
+    t_roof = max(flop / (pk["bf16_tflops"] * 1e12), nbytes / (pk["hbm_gbs"] * 1e9))
+    return {"value": round(t_roof / times["P"], 6), "unit": "fraction of measured peak", "cores": ncpu,
+            "kind": "port", "gflops": {k: round(flop / t / 1e9, 1) for k, t in times.items()},
+            "ms": {k: round(t * 1e3, 2) for k, t in times.items()},
+            "sample": f"P / I / W at M=K={M}, B={B} in fp32 torch on {ncpu} threads of {model}"}
 
 
 def run_c3(args, world, rank, local):
@@ -872,7 +914,10 @@ def run_c3(args, world, rank, local):
             torch.cuda.empty_cache()
     big = [p for p in points if p["bound"] == "tensor" and p["M"] >= 4096]
     head = max(big, key=lambda p: p["frac"]) if big else max(points, key=lambda p: p["frac"])
-    return {"metric": "per-kernel microbench (configs[2]): fraction of roofline", "value": head["frac"],
+    extra = {}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        extra["cpu_baseline"] = _c3_cpu_line(head["M"], head["B"], pk)
+    return {**extra, "metric": "per-kernel microbench (configs[2]): fraction of roofline", "value": head["frac"],
             "unit": "fraction of measured peak", "n_gpus": 1, "steps": len(points), "warmup": 1,
             "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
@@ -897,6 +942,17 @@ def run_reference(args, world, rank):
                 "config": {"workload": "configs[4] wide: dims (1000,4096x6,4096), T=4, tanh (B=512 sample)"},
                 "cpu_baseline": cb,
                 "e2e": {"value": round(cb["value"], 1), "unit": "samples/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+    if args.config == "c3":
+        M, B = 4096, 8192
+        cb = _c3_cpu_line(M, B, peaks())
+        return {"metric": "per-kernel microbench (configs[2]): fraction of roofline", "value": cb["value"],
+                "unit": "fraction of measured peak", "n_gpus": world, "steps": 1, "warmup": 1,
+                "ms_per_step": cb["ms"]["P"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic", "impl": "reference",
+                "config": {"workload": f"configs[2] headline point: P at M=K={M}, B={B}, fp32 torch on the host"},
+                "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "fraction of measured peak", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
     if args.config in ("c4a", "c4b"):
         if args.config == "c4a":
