@@ -135,6 +135,7 @@ int grid_1d(long long n) {
 int launch_outer(void* out, const void* e, const void* x, int M, int K, int B, int groups, float alpha,
                  bool bact, bool delta, int accumulate, int act, int dtype, cudaStream_t s) {
   if (M <= 0 || K <= 0 || groups <= 0) return IPC_OK;
+  if (B <= 0 && !delta) return IPC_OK;  // W + alpha * (empty sum) = W; a delta still writes its zeros
   dim3 grid((K + OT_COLS - 1) / OT_COLS, (M + OT_ROWS - 1) / OT_ROWS, groups);
   if (grid.y > 65535u || grid.z > 65535u) return set_error(IPC_ERR_ARG, "outer update grid too large");
   const int vec_ok = (K % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
