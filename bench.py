@@ -445,21 +445,39 @@ def run_c5(args, world, rank, local):
             "peak_kind": "sustained (kernels timed inside a ~0.1 s step)",
             "kernel": "tc_gemm_kernel (all GEMMs of the step; per-rank FLOP / per-step time, comms included)",
             "algorithmic_flop_per_step_per_rank": flop_rank}
-    # e2e: the public API with the batch in pinned host memory, copied in every step, a metric read back
+    # e2e: the public API with the batch in pinned host memory, copied in every step on a copy stream
+    # (double-buffered: step i's copy overlaps step i-1), a metric read back every step
     x_h = pool[0][0].cpu().pin_memory()
     y_h = pool[0][1].cpu().pin_memory()
-    xd, yd = torch.empty_like(pool[0][0]), torch.empty_like(pool[0][1])
-    n_e2e = max(1, min(args.steps, 3))
+    ring = [(torch.empty_like(pool[0][0]), torch.empty_like(pool[0][1])) for _ in range(2)]
+    n_e2e = max(3, min(args.steps, 8))
     metric_h = torch.empty(n_e2e, dtype=torch.float32).pin_memory()
+    copy = torch.cuda.Stream(dev)
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    for s_ in range(2):
+        free[s_].record(stream)
+
+    def h2d(slot):
+        with torch.cuda.stream(copy):
+            copy.wait_event(free[slot])
+            ring[slot][0].copy_(x_h, non_blocking=True)
+            ring[slot][1].copy_(y_h, non_blocking=True)
+            ready[slot].record(copy)
+
     barrier(world)
     torch.cuda.synchronize(dev)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
+    h2d(0)
     for i in range(n_e2e):
-        xd.copy_(x_h, non_blocking=True)
-        yd.copy_(y_h, non_blocking=True)
+        slot = i % 2
+        if i + 1 < n_e2e:
+            h2d((i + 1) % 2)
+        stream.wait_event(ready[slot])
         restore()
-        dp.train_step(xd, yd, T=T)
+        dp.train_step(*ring[slot], T=T)
+        free[slot].record(stream)
         metric_h[i:i + 1].copy_((dp.model.e[0].float() ** 2).mean().reshape(1), non_blocking=True)
     f1.record(stream)
     torch.cuda.synchronize(dev)
@@ -475,7 +493,9 @@ def run_c5(args, world, rank, local):
         "roofline": roof,
         "e2e": {"value": round(n_e2e * Bg / (ms_e2e * 1e-3), 1), "unit": "samples/s",
                 "h2d_bytes_per_step": int(x_h.numel() + y_h.numel()) * 2, "d2h_bytes_per_step": 4,
-                "path": "DataParallelIPC.train_step on a batch copied from pinned host memory each step"},
+                "steps": n_e2e,
+                "path": "DataParallelIPC.train_step on a batch copied from pinned host memory each step "
+                        "(copy stream, double-buffered), a metric read back each step"},
         "gpu_launches": int(launches), "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -577,9 +597,19 @@ def run_c4b(args, world, rank, local):
     # HBM the fused step cannot avoid: each network-step reads its batch (x_L and the one-hot target)
     need_net = (dims[-1] + dims[0]) * B * 2
     need_gbs = need_net * units / (avg_ms * 1e-3) / 1e9
-    roof = {"bound": "tensor", "achieved": round(tfs, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-            "frac": round(tfs / pk["bf16_tflops"], 4),
-            "traffic": TRAFFIC_PER_STEP.get(("c4b", 1)) and round(TRAFFIC_PER_STEP[("c4b", 1)] * units),
+    # the bound is the larger ideal time per network-step (the rule of the other configs): by the
+    # per-operator byte formula the batched form is HBM-bound (AI ~31 FLOP/B)
+    gbs = bytes_net * units / (avg_ms * 1e-3) / 1e9
+    hbm_bound = bytes_net / (pk["hbm_gbs"] * 1e9) >= flop_net / (pk["bf16_tflops"] * 1e12)
+    roof = {"bound": "hbm" if hbm_bound else "tensor",
+            "achieved": round(gbs, 1) if hbm_bound else round(tfs, 2),
+            "peak": pk["hbm_gbs"] if hbm_bound else pk["bf16_tflops"],
+            "unit": "GB/s" if hbm_bound else "TFLOP/s",
+            "frac": round(gbs / pk["hbm_gbs"], 4) if hbm_bound else round(tfs / pk["bf16_tflops"], 4),
+            "tensor_frac": round(tfs / pk["bf16_tflops"], 4),
+            # profiles/net_kernel_c4b_296nets.md: per network and launch, 203,264 B of batch per step plus
+            # 118,651 B (weights read) + 288,058 B (written back) once, scaled to this launch
+            "traffic": round(nets * (full[0][1] * 203264 + 118651 + 288058)),
             "peak_source": pk["source"], "kernel": "net_kernel (ipc_net_train, nets per launch = %d)" % nets,
             "algorithmic_flop_per_network_step": flop_net, "network_steps_per_launch": units,
             "avg_launch_ms": round(avg_ms, 4),
