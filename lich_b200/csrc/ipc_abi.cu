@@ -269,12 +269,14 @@ int ipc_selftest_barrier_timeout(void* sync, int limit_us, void* stream) {
 int ipc_device_status(int* status, int clear) {
   int rc = require_sm100();
   if (rc) return rc;
-  int tc = 0, wide = 0;
+  int tc = 0, wide = 0, net = 0;
   rc = read_device_status(&tc, clear);
   if (rc) return rc;
   rc = read_wide_status(&wide, clear);
   if (rc) return rc;
-  if (status) *status = tc != 0 ? tc : wide;
+  rc = read_net_status(&net, clear);
+  if (rc) return rc;
+  if (status) *status = tc != 0 ? tc : (wide != 0 ? wide : net);
   return IPC_OK;
 }
 

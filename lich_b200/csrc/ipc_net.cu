@@ -81,7 +81,7 @@ struct NetParams {
   // shared-memory layout, byte offsets
   int o_w[MAXL], o_x[MAXL], o_a[MAXL], o_e[MAXL];
   int o_ge[MAX_OWN], o_ga[MAX_OWN];
-  int o_mu, o_wt, o_al, o_recv, o_gt;
+  int o_mu, o_wt, o_al, o_recv, o_gt, o_bar;
   int wtld, ald, gld;
   int smem_bytes;
 };
@@ -121,6 +121,52 @@ __device__ __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint3
   }
 }
 
+// First error a bounded wait of this kernel recorded (read by ipc_device_status).
+__device__ int g_net_status = 0;
+constexpr long long NET_WAIT_NS = 2000000000LL;
+
+__device__ __forceinline__ void nbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void nbar_expect(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// Bounded wait on a phase of a local mbarrier; on expiry the status word is set and the caller goes
+// on (every CTA keeps reaching every cluster barrier, so the launch still ends).
+__device__ __forceinline__ void nbar_wait(uint32_t bar, uint32_t parity) {
+  long long tstart = -1;
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return;
+    long long now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    if (tstart < 0) tstart = now;
+    if (now - tstart > NET_WAIT_NS) {
+      atomicCAS(&g_net_status, 0, IPC_ERR_TIMEOUT);
+      return;
+    }
+  }
+}
+// Bulk copy of `bytes` from this CTA's shared memory to the same offset in CTA `rank`, completing
+// `bytes` of the transaction count of that CTA's mbarrier `bar` (a shared::cta offset here).
+__device__ __forceinline__ void bulk_to_peer(uint32_t local, uint32_t bytes, uint32_t bar, uint32_t rank) {
+  uint32_t dst, rbar;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(local), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(bar), "r"(rank));
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "r"(local), "r"(bytes), "r"(rbar)
+      : "memory");
+}
+
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
@@ -132,15 +178,6 @@ __device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void st_dsmem_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared::cluster.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
-}
-__device__ __forceinline__ void st_dsmem_f2(uint32_t addr, float a, float b) {
-  asm volatile("st.shared::cluster.v2.f32 [%0], {%1,%2};\n" ::"r"(addr), "f"(a), "f"(b) : "memory");
-}
-__device__ __forceinline__ void st_dsmem_u32(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ void st_dsmem_u16(uint32_t addr, uint16_t v) {
-  asm volatile("st.shared::cluster.u16 [%0], %1;\n" ::"r"(addr), "h"(v) : "memory");
 }
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
@@ -319,6 +356,19 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
     reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
   __syncthreads();
 
+  // Hidden-weight replicas: the owner of layer l (CTA l % C) updates its own copy and bulk-copies
+  // the tile to every peer; each CTA's mbarrier expects, per step, the bytes of the layers it does
+  // not own, and is waited on before the replicas are next read.
+  const uint32_t wbar = sbase + p.o_bar;
+  uint32_t incoming = 0;
+  for (int l = 0; l < Lt; ++l)
+    if (l % C != cta) incoming += (uint32_t)(p.rows16[l] * WLD * (int)sizeof(T));
+  if (p.update_weights && threadIdx.x == 0) {
+    nbar_init(wbar, 1);
+    nbar_expect(wbar, incoming);  // phase 0: the replicas of step 0
+  }
+  __syncthreads();
+
   // this network's global slabs
   auto gw = [&](int l) { return p.w[l] + (long long)net * p.dims[l] * p.dims[l + 1]; };
   auto gx = [&](int l) { return p.x[l] + (long long)net * p.dims[l] * B; };
@@ -422,6 +472,10 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
         s1 += v.y;
       }
       U32(p.o_mu, sw<NCOL>(r, j)) = r < dT ? bits2<T>(s0, s1) : 0u;
+    }
+    if (p.update_weights && step > 0 && threadIdx.x == 0) {
+      nbar_wait(wbar, (uint32_t)((step - 1) & 1));  // last step's replicas have landed
+      nbar_expect(wbar, incoming);                  // this step's
     }
     __syncthreads();
     trace(step, 3);
@@ -647,29 +701,37 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
               seg[j] = h ? a1 : a0;
             }
             const int rr = mt * 16 + gq + 8 * h;
-            if (tq < 2 && rr < p.dims[l] && nt * 8 < cols) {
-              const uint32_t a = sbase + p.o_w[l] + 2 * (rr * WLD + nt * 8);
-              const uint4 sv = make_uint4(seg[0], seg[1], seg[2], seg[3]);
-              for (int cc = 0; cc < C; ++cc) st_dsmem_v4(mapa(a, cc), sv);
-            }
+            if (tq < 2 && rr < p.dims[l] && nt * 8 < cols)
+              *reinterpret_cast<uint4*>(smem + p.o_w[l] + 2 * (rr * WLD + nt * 8)) =
+                  make_uint4(seg[0], seg[1], seg[2], seg[3]);
           } else {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int rr = mt * 16 + gq + 8 * h;
               if (rr >= p.dims[l] || n >= cols) continue;
               const int idx = rr * WLD + n;
-              const uint32_t a = sbase + p.o_w[l] + 2 * idx;
               if (n + 1 < cols) {
                 float w0, w1;
                 unpack2<T>(U32(p.o_w[l], idx), w0, w1);
-                const uint32_t v = bits2<T>(w0 + p.alpha * acc[2 * h], w1 + p.alpha * acc[2 * h + 1]);
-                for (int cc = 0; cc < C; ++cc) st_dsmem_u32(mapa(a, cc), v);
+                U32(p.o_w[l], idx) = bits2<T>(w0 + p.alpha * acc[2 * h], w1 + p.alpha * acc[2 * h + 1]);
               } else {
-                const uint16_t v = bits<T>(St<T>::ld(S(p.o_w[l])[idx]) + p.alpha * acc[2 * h]);
-                for (int cc = 0; cc < C; ++cc) st_dsmem_u16(mapa(a, cc), v);
+                S(p.o_w[l])[idx] = St<T>::st(St<T>::ld(S(p.o_w[l])[idx]) + p.alpha * acc[2 * h]);
               }
             }
           }
+        }
+      }
+      // the new tiles of the owned layers go to every peer as one bulk copy each (the copy engine
+      // reads them after the generic stores above are made visible to the async proxy)
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        for (int slot = 0; slot < p.nown; ++slot) {
+          const int l = cta + slot * C;
+          if (l >= Lt) break;
+          const uint32_t bytes = (uint32_t)(p.rows16[l] * WLD * (int)sizeof(T));
+          for (int cc = 0; cc < C; ++cc)
+            if (cc != cta) bulk_to_peer(sbase + p.o_w[l], bytes, wbar, (uint32_t)cc);
         }
       }
       trace(step, 9);
@@ -693,7 +755,9 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
 
   // ---- outputs: states / errors of the owned columns, weights, the trained batch ----
   if (p.update_weights) {
-    cluster_sync_all();  // every replica holds every owner's new tiles
+    if (p.steps > 0 && threadIdx.x == 0) nbar_wait(wbar, (uint32_t)((p.steps - 1) & 1));
+    __syncthreads();
+    cluster_sync_all();  // every replica holds every owner's new tiles; no copy is still in flight
     if (cta == 0) {
       for (int l = 0; l < Lt; ++l) {
         const int cols = p.dims[l + 1];
@@ -757,6 +821,7 @@ int make_layout(NetParams<T>& p, int C, int NCOL) {
   p.o_al = take(p.KSP * p.ald * es);
   p.o_recv = take(C * p.rows16[Lt] * NCOL * 4);
   p.o_gt = take(p.rows16[Lt] * p.gld * es);
+  p.o_bar = take(16);  // mbarrier counting the hidden-weight replicas arriving from their owners
   for (int s = 0; s < p.nown; ++s) {
     p.o_ge[s] = take(64 * p.gld * es);
     p.o_ga[s] = take(64 * p.gld * es);
@@ -887,6 +952,20 @@ namespace ipc {
 bool wide_net_fits(const ipc_net_t* net);
 int wide_net_smem(const ipc_net_t* net);
 int wide_net_train(const ipc_net_t* net, const ipc_net_run_t* run, cudaStream_t s);
+}  // namespace ipc
+
+namespace ipc {
+int read_net_status(int* status, int clear) {
+  int v = 0;
+  cudaError_t err = cudaMemcpyFromSymbol(&v, g_net_status, sizeof(int));
+  if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "device status read: %s", cudaGetErrorString(err));
+  if (clear && v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_net_status, &zero, sizeof(int));
+  }
+  if (status) *status = v;
+  return IPC_OK;
+}
 }  // namespace ipc
 
 extern "C" int ipc_net_plan(const ipc_net_t* net, int cluster, int* cluster_out, int* smem_bytes_out) {

@@ -16,6 +16,8 @@ int launch_tc(const GemmArgs& p, int mode, int act, int dtype, cudaStream_t s, f
 int read_device_status(int* status, int clear);
 // The same for the bounded grid barriers of the wide small-batch step kernel (ipc_widenet.cu).
 int read_wide_status(int* status, int clear);
+// The same for the bounded mbarrier waits of the persistent cluster kernel (ipc_net.cu).
+int read_net_status(int* status, int clear);
 // Launch the barrier-timeout self-test (ipc_widenet.cu).
 int wide_selftest_timeout(void* sync, int limit_us, cudaStream_t s);
 }  // namespace ipc
