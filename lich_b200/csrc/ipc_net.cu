@@ -81,7 +81,7 @@ struct NetParams {
   // shared-memory layout, byte offsets
   int o_w[MAXL], o_x[MAXL], o_a[MAXL], o_e[MAXL];
   int o_ge[MAX_OWN], o_ga[MAX_OWN];
-  int o_mu, o_wt, o_al, o_recv, o_gt, o_bar;
+  int o_mu, o_wt, o_al, o_recv, o_gt, o_bar, o_obar, nblk;
   int wtld, ald, gld;
   int smem_bytes;
 };
@@ -164,6 +164,18 @@ __device__ __forceinline__ void bulk_to_peer(uint32_t local, uint32_t bytes, uin
   asm volatile(
       "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
       "r"(local), "r"(bytes), "r"(rbar)
+      : "memory");
+}
+
+// Bulk copy of `bytes` from this CTA's shared memory (`src`) to offset `dst` of CTA `rank`'s shared
+// memory, completing `bytes` of that CTA's mbarrier `bar` (dst and bar given as local offsets).
+__device__ __forceinline__ void bulk_to(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar, uint32_t rank) {
+  uint32_t rdst, rbar;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(dst), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(bar), "r"(rank));
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(rdst),
+      "r"(src), "r"(bytes), "r"(rbar)
       : "memory");
 }
 
@@ -303,6 +315,26 @@ __device__ __forceinline__ void frag_b_nk(uint32_t (&r)[2], uint32_t base, int l
   const int q = (lane >> 3) & 1, j = lane & 7;
   ldsm_x2(r, base + 2 * ((n0 + j) * ld + k0 + q * 8));
 }
+// Gathered operands of the weight update are "blocked": [k / NCOL][R rows][NCOL], block c being a
+// byte copy of CTA c's swizzled state tile (row r, 8-column chunk j stored at chunk j ^ s(r)).
+template <int NCOL>
+__device__ __forceinline__ int blk_off(int R, int row, int k) {
+  constexpr int VPR = NCOL / 8;
+  const int s = ((row * VPR) >> 3) & (VPR - 1);
+  return ((k / NCOL) * R + row) * NCOL + ((((k % NCOL) >> 3) ^ s) << 3);
+}
+// A fragment (16x16) of a blocked [m][k] operand.
+template <int NCOL>
+__device__ __forceinline__ void frag_a_blk(uint32_t (&r)[4], uint32_t base, int R, int m0, int k0, int lane) {
+  const int q = lane >> 3, j = lane & 7;
+  ldsm_x4(r, base + 2 * blk_off<NCOL>(R, m0 + j + (q & 1) * 8, k0 + (q >> 1) * 8));
+}
+// B fragment (16x8) of a blocked [n][k] operand.
+template <int NCOL>
+__device__ __forceinline__ void frag_b_blk(uint32_t (&r)[2], uint32_t base, int R, int k0, int n0, int lane) {
+  const int q = (lane >> 3) & 1, j = lane & 7;
+  ldsm_x2(r, base + 2 * blk_off<NCOL>(R, n0 + j, k0 + q * 8));
+}
 
 // --------------------------------------------------------- kernel helpers
 // cp.async rows [0, rows) x columns [0, ncol) of a row-major global matrix
@@ -363,9 +395,19 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
   uint32_t incoming = 0;
   for (int l = 0; l < Lt; ++l)
     if (l % C != cta) incoming += (uint32_t)(p.rows16[l] * WLD * (int)sizeof(T));
+  // Weight-update operands: every CTA sends its e[L-1] tile to every CTA and its e[l], f(x[l+1])
+  // tiles to the owner of layer l, one bulk copy each; obar expects this CTA's share per step.
+  const uint32_t obar = sbase + p.o_obar;
+  uint32_t operands = (uint32_t)(C * p.rows16[Lt] * NCOL * (int)sizeof(T));
+  for (int slot = 0; slot < p.nown; ++slot) {
+    const int l = cta + slot * C;
+    if (l < Lt) operands += (uint32_t)(C * (p.rows16[l] + p.rows16[l + 1]) * NCOL * (int)sizeof(T));
+  }
   if (p.update_weights && threadIdx.x == 0) {
     nbar_init(wbar, 1);
     nbar_expect(wbar, incoming);  // phase 0: the replicas of step 0
+    nbar_init(obar, 1);
+    nbar_expect(obar, operands);  // phase 0: the operands of step 0
   }
   __syncthreads();
 
@@ -605,30 +647,26 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
 
     const bool more = step + 1 < p.steps;
     if (p.update_weights) {
-      // ---- push the weight-update operands (DSMEM stores only) ----
-      {
-        // e[L-1], owned columns -> every CTA's E_top[:, c0 .. c0+NCOL)
-        const int n_top = p.rows16[Lt] * VPR;
-        for (int it = threadIdx.x; it < n_top * C; it += NET_THREADS) {
-          const int cc = it / n_top, rem = it % n_top, r = rem / VPR, j = rem % VPR;
-          const uint4 v = *reinterpret_cast<const uint4*>(smem + p.o_e[Lt] + 2 * sw<NCOL>(r, 8 * j));
-          st_dsmem_v4(mapa(sbase + p.o_gt + 2 * (r * p.gld + c0 + 8 * j), cc), v);
+      // ---- send the weight-update operands: one bulk copy per tile and destination ----
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the state tiles, to the copy engine
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        const uint32_t top = (uint32_t)(p.rows16[Lt] * NCOL * (int)sizeof(T));
+        for (int cc = 0; cc < C; ++cc)  // e[L-1] -> every CTA's E_top, block cta
+          bulk_to(sbase + p.o_gt + (uint32_t)cta * top, sbase + p.o_e[Lt], top, obar, (uint32_t)cc);
+        const uint32_t blk = (uint32_t)(64 * NCOL * (int)sizeof(T));
+        for (int l = 0; l < Lt; ++l) {  // e[l], f(x[l+1]) -> the owner of layer l, block cta
+          const uint32_t owner = (uint32_t)(l % C), slot = (uint32_t)(l / C);
+          bulk_to(sbase + p.o_ge[slot] + (uint32_t)cta * blk, sbase + p.o_e[l],
+                  (uint32_t)(p.rows16[l] * NCOL * (int)sizeof(T)), obar, owner);
+          bulk_to(sbase + p.o_ga[slot] + (uint32_t)cta * blk, sbase + p.o_a[l + 1],
+                  (uint32_t)(p.rows16[l + 1] * NCOL * (int)sizeof(T)), obar, owner);
         }
-        // e[l], f(x[l+1]) owned columns -> the CTA owning hidden layer l
-        for (int l = 0; l < Lt; ++l) {
-          const int owner = l % C, slot = l / C;
-          const int ne = p.rows16[l] * VPR, na = p.rows16[l + 1] * VPR;
-          for (int it = threadIdx.x; it < ne + na; it += NET_THREADS) {
-            const bool isE = it < ne;
-            const int rem = isE ? it : it - ne, r = rem / VPR, j = rem % VPR;
-            const int src_off = isE ? p.o_e[l] : p.o_a[l + 1];
-            const int dst_off = isE ? p.o_ge[slot] : p.o_ga[slot];
-            const uint4 v = *reinterpret_cast<const uint4*>(smem + src_off + 2 * sw<NCOL>(r, 8 * j));
-            st_dsmem_v4(mapa(sbase + dst_off + 2 * (r * p.gld + c0 + 8 * j), owner), v);
-          }
-        }
+        // (B) this CTA's update operands have arrived: every peer finished its iterations
+        nbar_wait(obar, (uint32_t)(step & 1));
+        nbar_expect(obar, operands);  // the next step's
       }
-      cluster_sync_all();  // (B) every CTA holds the operands of the layers it updates
+      __syncthreads();
       trace(step, 7);
       // ---- input layer: W[L-1][:, own K] += alpha E[L-1] f(x_L)^T (local slice) ----
       {
@@ -639,7 +677,7 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
           float acc[4] = {0.f, 0.f, 0.f, 0.f};
           for (int b0 = 0; b0 < B16; b0 += 16) {
             uint32_t af[4], bf[2];
-            frag_a(af, sbase + p.o_gt, p.gld, mt * 16, b0, lane);
+            frag_a_blk<NCOL>(af, sbase + p.o_gt, p.rows16[Lt], mt * 16, b0, lane);
             frag_b_nk(bf, sbase + p.o_al, p.ald, b0, nt * 8, lane);
             mma<T>(acc, af, bf[0], bf[1]);
           }
@@ -674,8 +712,8 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
           float acc[4] = {0.f, 0.f, 0.f, 0.f};
           for (int b0 = 0; b0 < B16; b0 += 16) {
             uint32_t af[4], bf[2];
-            frag_a(af, sbase + p.o_ge[slot], p.gld, mt * 16, b0, lane);
-            frag_b_nk(bf, sbase + p.o_ga[slot], p.gld, b0, nt * 8, lane);
+            frag_a_blk<NCOL>(af, sbase + p.o_ge[slot], 64, mt * 16, b0, lane);
+            frag_b_blk<NCOL>(bf, sbase + p.o_ga[slot], 64, b0, nt * 8, lane);
             mma<T>(acc, af, bf[0], bf[1]);
           }
           const int n = nt * 8 + 2 * tq;
@@ -820,11 +858,14 @@ int make_layout(NetParams<T>& p, int C, int NCOL) {
   p.o_wt = take(p.rows16[Lt] * p.wtld * es);
   p.o_al = take(p.KSP * p.ald * es);
   p.o_recv = take(C * p.rows16[Lt] * NCOL * 4);
-  p.o_gt = take(p.rows16[Lt] * p.gld * es);
-  p.o_bar = take(16);  // mbarrier counting the hidden-weight replicas arriving from their owners
+  // gathered weight-update operands, one block per source CTA plus zero blocks up to B rounded to 16
+  p.nblk = ((p.B + 15) / 16 * 16) / NCOL;
+  p.o_gt = take(p.nblk * p.rows16[Lt] * NCOL * es);
+  p.o_bar = take(16);   // mbarrier counting the hidden-weight replicas arriving from their owners
+  p.o_obar = take(16);  // mbarrier counting the gathered operands of this CTA's updates
   for (int s = 0; s < p.nown; ++s) {
-    p.o_ge[s] = take(64 * p.gld * es);
-    p.o_ga[s] = take(64 * p.gld * es);
+    p.o_ge[s] = take(p.nblk * 64 * NCOL * es);
+    p.o_ga[s] = take(p.nblk * 64 * NCOL * es);
   }
   p.smem_bytes = off;
   return off;
