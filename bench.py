@@ -314,8 +314,8 @@ def run_c2(args, world, rank, local):
 # ncu dram__bytes_read.sum + dram__bytes_write.sum per training step of the persistent
 # kernel, from the captures summarised in profiles/ (filled in after each capture).
 TRAFFIC_PER_STEP: dict = {
-    # profiles/net_kernel_c2_depth6.md: 10,393,856 B read + 0 B written over a 50-step launch
-    ("c2", 6): 10393856 / 50,
+    # profiles/net_kernel_c2_depth6.md: 10,404,864 B read + 0 B written over a 50-step launch
+    ("c2", 6): 10404864 / 50,
 }
 
 
@@ -608,8 +608,8 @@ def run_c4b(args, world, rank, local):
             "frac": round(gbs / pk["hbm_gbs"], 4) if hbm_bound else round(tfs / pk["bf16_tflops"], 4),
             "tensor_frac": round(tfs / pk["bf16_tflops"], 4),
             # profiles/net_kernel_c4b_296nets.md: per network and launch, 203,264 B of batch per step plus
-            # 118,651 B (weights read) + 288,058 B (written back) once, scaled to this launch
-            "traffic": round(nets * (full[0][1] * 203264 + 118651 + 288058)),
+            # 118,690 B (weights read) + 279,658 B (written back) once, scaled to this launch
+            "traffic": round(nets * (full[0][1] * 203264 + 118690 + 279658)),
             "peak_source": pk["source"], "kernel": "net_kernel (ipc_net_train, nets per launch = %d)" % nets,
             "algorithmic_flop_per_network_step": flop_net, "network_steps_per_launch": units,
             "avg_launch_ms": round(avg_ms, 4),
