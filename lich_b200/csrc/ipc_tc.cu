@@ -242,6 +242,41 @@ __device__ __forceinline__ void epi8(const TcParams& p, int g, int m, int n, con
   }
 }
 
+// The same epilogue with the row's in/out operand already in registers (loaded before the
+// accumulator was ready): P av = X_lo; I av = E, xv = X; W av = W.
+template <typename T, int ACT, int MODE>
+__device__ __forceinline__ void epi8_pre(const TcParams& p, int g, int m, int n, const float (&acc)[8], uint4 av,
+                                         uint4 xv) {
+  const long long idx = (long long)m * p.ld_out + n;
+  const T* ah = reinterpret_cast<const T*>(&av);
+  if constexpr (MODE == MODE_P) {
+    float ev[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ev[j] = St<T>::ld(ah[j]) - rnd<T>(acc[j]);
+    Vec8<T>::st(reinterpret_cast<T*>(p.out) + g * p.gs_out + idx, ev);
+  } else if constexpr (MODE == MODE_I) {
+    const T* xh = reinterpret_cast<const T*>(&xv);
+    float xn[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float x0 = St<T>::ld(xh[j]);
+      xn[j] = x0 + p.scale * (-St<T>::ld(ah[j]) + act_df<ACT>(x0) * acc[j]);
+    }
+    Vec8<T>::st(reinterpret_cast<T*>(p.out) + g * p.gs_out + idx, xn);
+    if (p.aux2 != nullptr) {
+      float an[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) an[j] = act_f<ACT>(p.a_out_from_stored ? rnd<T>(xn[j]) : xn[j]);
+      Vec8<T>::st(reinterpret_cast<T*>(p.aux2) + g * p.gs_aux2 + idx, an);
+    }
+  } else if constexpr (MODE == MODE_W) {
+    float wv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wv[j] = St<T>::ld(ah[j]) + p.scale * acc[j];
+    Vec8<T>::st(reinterpret_cast<T*>(p.out) + g * p.gs_out + idx, wv);
+  }
+}
+
 template <typename T, int ACT, int MODE, int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -373,16 +408,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int acc = 0;
     uint32_t aphase = 0;
+    // P and W (one in/out stream, a light epilogue): the row's operand is loaded before the
+    // accumulator is ready, so its memory latency overlaps the tile's MMAs.  I keeps a rolled chunk
+    // loop: its epilogue (f, f') unrolled 8 times crowds the instruction cache the MMA issuer shares.
+    constexpr int PF = (MODE == MODE_P || MODE == MODE_W) ? BN : 0;
+    constexpr int NPF = PF / 8 > 0 ? PF / 8 : 1;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
+      int g, m0, n0, sp;
+      tile_coords(p, t, BN, g, m0, n0, sp);
+      const int m = m0 + 32 * q + lane;
+      uint4 pfa[NPF], pfx[MODE == MODE_I ? NPF : 1];
+      const bool pre = PF > 0 && p.splits == 1 && m < p.Mg;
+      if (pre) {
+        const long long row = (long long)m * p.ld_out;
+#pragma unroll
+        for (int v = 0; v < PF / 8; ++v) {
+          const int n = n0 + 8 * v;
+          if (n < p.Ng) {
+            if constexpr (MODE == MODE_P)
+              pfa[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + row + n);
+            else if constexpr (MODE == MODE_W)
+              pfa[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.out) + g * p.gs_out + row + n);
+            else if constexpr (MODE == MODE_I) {
+              pfa[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + row + n);
+              pfx[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.out) + g * p.gs_out + row + n);
+            }
+          }
+        }
+      }
       const bool ok = mbar_wait(tfull0 + 8 * acc, aphase, abort_flag);
       __syncwarp();
       if (!ok) break;
       tc_fence_after();
-      int g, m0, n0, sp;
-      tile_coords(p, t, BN, g, m0, n0, sp);
-      const int m = m0 + 32 * q + lane;
       const uint32_t trow = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
-#pragma unroll 1
+#pragma unroll(PF > 0 ? BN / 32 : 1)
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t raw[32];
         tmem_ld32(trow + 32 * c, raw);
@@ -390,8 +449,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             const int n = n0 + 32 * c + 8 * v;
+            const int vi = 4 * c + v;  // vector index within the row
             if (n < p.Ng) {
-              if (p.splits > 1) {  // fp32 partial of this K range; the reduce pass applies the epilogue
+              if (pre && vi < PF / 8) {
+                float a8[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[8 * v + j]);
+                epi8_pre<T, ACT, MODE>(p, g, m, n, a8, pfa[vi < NPF ? vi : 0],
+                                       pfx[MODE == MODE_I && vi < NPF ? vi : 0]);
+              } else if (p.splits > 1) {  // fp32 partial of this K range; the reduce pass applies the epilogue
                 float4* dst = reinterpret_cast<float4*>(
                     p.ws + (((long long)sp * p.groups + g) * p.Mg + m) * (long long)p.Ng + n);
                 dst[0] = make_float4(__uint_as_float(raw[8 * v]), __uint_as_float(raw[8 * v + 1]),
