@@ -186,7 +186,8 @@ struct Vec8 {
   }
 };
 
-// Fused epilogue for 8 consecutive columns [n, n+8) of output row m.
+// Fused epilogue for 8 consecutive columns [n, n+8) of output row m.  f and f' use the MUFU forms
+// (relative error near 2^-11, one fp16 rounding step): every result here is stored in 16 bits.
 template <typename T, int ACT, int MODE>
 __device__ __forceinline__ void epi8(const TcParams& p, int g, int m, int n, const float (&acc)[8]) {
   const long long idx = (long long)m * p.ld_out + n;
@@ -202,12 +203,12 @@ __device__ __forceinline__ void epi8(const TcParams& p, int g, int m, int n, con
     Vec8<T>::ld(xp, xv);
     Vec8<T>::ld(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + idx, ev);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) xn[j] = xv[j] + p.scale * (-ev[j] + act_df<ACT>(xv[j]) * acc[j]);
+    for (int j = 0; j < 8; ++j) xn[j] = xv[j] + p.scale * (-ev[j] + act_df_hw<ACT>(xv[j]) * acc[j]);
     Vec8<T>::st(xp, xn);
     if (p.aux2 != nullptr) {
       float an[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) an[j] = act_f<ACT>(p.a_out_from_stored ? rnd<T>(xn[j]) : xn[j]);
+      for (int j = 0; j < 8; ++j) an[j] = act_f_hw<ACT>(p.a_out_from_stored ? rnd<T>(xn[j]) : xn[j]);
       Vec8<T>::st(reinterpret_cast<T*>(p.aux2) + g * p.gs_aux2 + idx, an);
     }
   } else if constexpr (MODE == MODE_W) {
@@ -236,7 +237,7 @@ __device__ __forceinline__ void epi8(const TcParams& p, int g, int m, int n, con
     if (p.aux2 != nullptr) {
       float an[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) an[j] = act_f<ACT>(rnd<T>(acc[j]));
+      for (int j = 0; j < 8; ++j) an[j] = act_f_hw<ACT>(rnd<T>(acc[j]));
       Vec8<T>::st(reinterpret_cast<T*>(p.aux2) + g * p.gs_aux2 + idx, an);
     }
   }
@@ -260,13 +261,13 @@ __device__ __forceinline__ void epi8_pre(const TcParams& p, int g, int m, int n,
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float x0 = St<T>::ld(xh[j]);
-      xn[j] = x0 + p.scale * (-St<T>::ld(ah[j]) + act_df<ACT>(x0) * acc[j]);
+      xn[j] = x0 + p.scale * (-St<T>::ld(ah[j]) + act_df_hw<ACT>(x0) * acc[j]);
     }
     Vec8<T>::st(reinterpret_cast<T*>(p.out) + g * p.gs_out + idx, xn);
     if (p.aux2 != nullptr) {
       float an[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) an[j] = act_f<ACT>(p.a_out_from_stored ? rnd<T>(xn[j]) : xn[j]);
+      for (int j = 0; j < 8; ++j) an[j] = act_f_hw<ACT>(p.a_out_from_stored ? rnd<T>(xn[j]) : xn[j]);
       Vec8<T>::st(reinterpret_cast<T*>(p.aux2) + g * p.gs_aux2 + idx, an);
     }
   } else if constexpr (MODE == MODE_W) {

@@ -3,7 +3,8 @@
 Every mode against the CPU oracle (storage rounding of the reference kernels,
 float64 accumulation), bound ``max|got - ref| / max|ref| <= 1e-2`` (the 16-bit
 gate); the fp32 weight delta ``<= 1e-3``.  Also: tails in M / N / K (TMA zero
-fill + epilogue masks), grouped launches, agreement with the mma.sync kernel,
+fill + epilogue masks), grouped launches, agreement with the mma.sync kernel
+(two storage rounding steps),
 and a clean device status word (no bounded wait expired).
 """
 import pytest
@@ -118,7 +119,9 @@ def test_tcgen05_agrees_with_mma_sync(dt):
         flags = N.FLAG_AOUT_STORED if mode == N.MODE_INFER else 0
         _, a, _ = _run(mode, 512, 768, 384, dt, "tcgen05", flags=flags, seed=9)
         _, b, _ = _run(mode, 512, 768, 384, dt, "simt", flags=flags, seed=9)
-        assert O.rel_inf(a["out"], b["out"]) <= 1e-3
+        # different summation orders, and the tensor-core epilogue evaluates f / f' with the MUFU
+        # forms (the mma.sync kernel with tanhf): stored outputs may differ by a storage rounding step
+        assert O.rel_inf(a["out"], b["out"]) <= (8e-3 if dt == torch.bfloat16 else 2e-3)
 
 
 def test_tcgen05_rejects_activated_operand_and_bad_strides():
