@@ -9,9 +9,12 @@
 //               tcgen05.mma.cta_group::1.kind::f16 (M = 128, N = BN, K = 16)
 //               into one of two TMEM accumulators (2 x BN fp32 columns);
 //               tcgen05.commit releases smem stages / publishes accumulators.
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator rows (thread = row),
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator rows (thread = row),
 //               the mode's fused element-wise epilogue, global stores; the
 //               second accumulator lets the next tile's MMAs run meanwhile.
+//               Two warps share each TMEM lane quarter (warp % 4), one per
+//               half of the BN accumulator columns, so a tile's epilogue
+//               keeps pace with its MMAs down to K ~ 1024.
 // All 32 lanes of warps 0 and 1 walk their loops (so the final CTA barrier is
 // reached convergently); lane 0 alone issues TMA, MMA and commits.
 // Operand orientation per mode (UMMA "K-major" = reduction dim contiguous):
@@ -46,7 +49,8 @@ namespace {
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;
 constexpr int TC_STAGES = 4;
-constexpr int TC_THREADS = 192;
+constexpr int TC_EPI_WARPS = 8;                     // two per TMEM lane quarter
+constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;  // TMA warp + MMA warp + epilogue
 constexpr long long TC_WAIT_NS = 2000000000LL;
 
 constexpr int TC_RASTER = 16;  // M-tiles per raster group: a wave covers ~16 x 9 tiles, both operands stay in L2
@@ -278,6 +282,21 @@ __device__ __forceinline__ void epi8_pre(const TcParams& p, int g, int m, int n,
   }
 }
 
+// I: one 32-column chunk of the row's E and X operands (4 vectors of 8).
+template <typename T>
+__device__ __forceinline__ void i_chunk_load(const TcParams& p, int g, int m, int n, uint4 (&ev)[4],
+                                             uint4 (&xv)[4]) {
+  if (m >= p.Mg) return;
+  const long long row = (long long)m * p.ld_out;
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    if (n + 8 * v < p.Ng) {
+      ev[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + row + n + 8 * v);
+      xv[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.out) + g * p.gs_out + row + n + 8 * v);
+    }
+  }
+}
+
 template <typename T, int ACT, int MODE, int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -310,7 +329,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
-      mbar_init(tempty0 + 8 * b, 128);
+      mbar_init(tempty0 + 8 * b, 32 * TC_EPI_WARPS);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -407,12 +426,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else {
     // ------------------------------- epilogue --------------------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    constexpr int HC = BN / 2;  // accumulator columns per epilogue warp
+    const int c_lo = ((warp - 2) >> 2) * HC;
     int acc = 0;
     uint32_t aphase = 0;
     // P and W (one in/out stream, a light epilogue): the row's operand is loaded before the
-    // accumulator is ready, so its memory latency overlaps the tile's MMAs.  I keeps a rolled chunk
-    // loop: its epilogue (f, f') unrolled 8 times crowds the instruction cache the MMA issuer shares.
-    constexpr int PF = (MODE == MODE_P || MODE == MODE_W) ? BN : 0;
+    // accumulator is ready, so its memory latency overlaps the tile's MMAs.  I (two input streams,
+    // f and f') keeps a rolled chunk loop that loads E and X one 32-column chunk ahead: unrolled, it
+    // would crowd the instruction cache the MMA issuer shares and spill.
+    constexpr int PF = (MODE == MODE_P || MODE == MODE_W) ? HC : 0;
     constexpr int NPF = PF / 8 > 0 ? PF / 8 : 1;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
       int g, m0, n0, sp;
@@ -424,7 +446,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const long long row = (long long)m * p.ld_out;
 #pragma unroll
         for (int v = 0; v < PF / 8; ++v) {
-          const int n = n0 + 8 * v;
+          const int n = n0 + c_lo + 8 * v;
           if (n < p.Ng) {
             if constexpr (MODE == MODE_P)
               pfa[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + row + n);
@@ -437,19 +459,48 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
       }
+      uint4 ce[4], cx[4];  // I: the current chunk's E and X, loaded one chunk ahead
+      if constexpr (MODE == MODE_I) i_chunk_load<T>(p, g, m, n0 + c_lo, ce, cx);
       const bool ok = mbar_wait(tfull0 + 8 * acc, aphase, abort_flag);
       __syncwarp();
       if (!ok) break;
       tc_fence_after();
       const uint32_t trow = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
-#pragma unroll(PF > 0 ? BN / 32 : 1)
-      for (int c = 0; c < BN / 32; ++c) {
+      if constexpr (MODE == MODE_I) {
+#pragma unroll 1
+        for (int c = 0; c < HC / 32; ++c) {
+          uint32_t raw[32];
+          tmem_ld32(trow + c_lo + 32 * c, raw);
+          uint4 ne[4], nx[4];
+          if (c + 1 < HC / 32) i_chunk_load<T>(p, g, m, n0 + c_lo + 32 * (c + 1), ne, nx);
+          if (m < p.Mg) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int n = n0 + c_lo + 32 * c + 8 * v;
+              if (n < p.Ng) {
+                float a8[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[8 * v + j]);
+                epi8_pre<T, ACT, MODE>(p, g, m, n, a8, ce[v], cx[v]);
+              }
+            }
+          }
+#pragma unroll
+          for (int v = 0; v < 4; ++v) { ce[v] = ne[v]; cx[v] = nx[v]; }
+        }
+        tc_fence_before();
+        mbar_arrive(tempty0 + 8 * acc);
+        if (++acc == 2) { acc = 0; aphase ^= 1; }
+        continue;
+      }
+#pragma unroll(PF > 0 ? HC / 32 : 1)
+      for (int c = 0; c < HC / 32; ++c) {
         uint32_t raw[32];
-        tmem_ld32(trow + 32 * c, raw);
+        tmem_ld32(trow + c_lo + 32 * c, raw);
         if (m < p.Mg) {
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
-            const int n = n0 + 32 * c + 8 * v;
+            const int n = n0 + c_lo + 32 * c + 8 * v;
             const int vi = 4 * c + v;  // vector index within the row
             if (n < p.Ng) {
               if (pre && vi < PF / 8) {
