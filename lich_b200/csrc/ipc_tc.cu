@@ -10,11 +10,17 @@
 //               into one of two TMEM accumulators (2 x BN fp32 columns);
 //               tcgen05.commit releases smem stages / publishes accumulators.
 //   warps 2..9  epilogue: tcgen05.ld of the accumulator rows (thread = row),
-//               the mode's fused element-wise epilogue, global stores; the
-//               second accumulator lets the next tile's MMAs run meanwhile.
-//               Two warps share each TMEM lane quarter (warp % 4), one per
-//               half of the BN accumulator columns, so a tile's epilogue
-//               keeps pace with its MMAs down to K ~ 1024.
+//               the mode's fused element-wise epilogue; the second
+//               accumulator lets the next tile's MMAs run meanwhile.  Two
+//               warps share each TMEM lane quarter (warp % 4), one per half
+//               of the BN accumulator columns.  P and W read their in/out
+//               operand (X_lo, W) with coalesced loads a tile ahead and pass
+//               it through a shared-memory transpose buffer (the row threads
+//               update it in place; coalesced stores write it back); I stages
+//               E and X with TMA loads and writes X / A_out with TMA stores.
+//               Either way a warp instruction moves whole 128-byte lines:
+//               row-per-thread global accesses would split it into 32
+//               requests.  F, dW (WD) and split-K partials store directly.
 // All 32 lanes of warps 0 and 1 walk their loops (so the final CTA barrier is
 // reached convergently); lane 0 alone issues TMA, MMA and commits.
 // Operand orientation per mode (UMMA "K-major" = reduction dim contiguous):
@@ -24,8 +30,9 @@
 // The B operand is taken as stored (a saved activation): applying f inside
 // the GEMM would repeat it M/128 times per element; callers materialise
 // f(X) once (ipc_activate, or the A_out of the state update / forward sweep).
-// Tails in M, N, K are handled by TMA zero fill and epilogue masks; inner
-// dimensions must be multiples of 8 elements (16-byte TMA strides).
+// Tails in M, N, K are handled by TMA zero fill, TMA store clipping and
+// epilogue masks; inner dimensions must be multiples of 8 elements (16-byte
+// TMA strides) and operands 16-byte aligned (else the generic kernel runs).
 //
 // Every mbarrier wait is bounded (about 2 s of %globaltimer); on expiry the
 // kernel records IPC_ERR_TIMEOUT in a device status word, every role stops
@@ -34,6 +41,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "ipc_common.cuh"
@@ -53,6 +61,13 @@ constexpr int TC_EPI_WARPS = 8;                     // two per TMEM lane quarter
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;  // TMA warp + MMA warp + epilogue
 constexpr long long TC_WAIT_NS = 2000000000LL;
 
+// Epilogue staging through shared memory (P, W, I without split-K): 4 KB per epilogue warp.  P / W
+// use it as one 32-row x 64-column transpose buffer (128-byte rows); I as two 2 KB slots, each holding
+// an E tile and an X tile of 32 rows x 16 columns (32-byte rows, TMA 32-byte swizzle).
+constexpr int EPI_SLOT = 2048;
+constexpr int EPI_WARP_BYTES = 2 * EPI_SLOT;
+constexpr int EPI_BYTES = TC_EPI_WARPS * EPI_WARP_BYTES;
+
 constexpr int TC_RASTER = 16;  // M-tiles per raster group: a wave covers ~16 x 9 tiles, both operands stay in L2
 
 struct TcParams {
@@ -71,6 +86,7 @@ struct TcParams {
   // fp32 partial tiles go to ws[split][group][m][n] and ws_reduce_kernel applies the epilogue
   int splits, kps;
   float* ws;
+  int staged;  // P / W / I: epilogue staged through shared memory with TMA loads and stores
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -142,6 +158,30 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+// Let a TMA load that is still in flight land (exit path after an aborted wait); bounded at 1 ms.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+  const long long t0 = now_ns();
+  while (!mbar_try(bar, parity) && now_ns() - t0 < 1000000LL) {
+  }
 }
 
 // Tile t -> (group, first row, first column).  Rows are walked in bands of
@@ -247,60 +287,53 @@ __device__ __forceinline__ void epi8(const TcParams& p, int g, int m, int n, con
   }
 }
 
-// The same epilogue with the row's in/out operand already in registers (loaded before the
-// accumulator was ready): P av = X_lo; I av = E, xv = X; W av = W.
-template <typename T, int ACT, int MODE>
-__device__ __forceinline__ void epi8_pre(const TcParams& p, int g, int m, int n, const float (&acc)[8], uint4 av,
-                                         uint4 xv) {
-  const long long idx = (long long)m * p.ld_out + n;
-  const T* ah = reinterpret_cast<const T*>(&av);
-  if constexpr (MODE == MODE_P) {
-    float ev[8];
+// The staged epilogue on one 16-byte vector (8 columns) of a thread's row: P e = x - cast(acc),
+// W w + alpha acc; I x + gamma (-e + f'(x) acc) and its activation.  Same arithmetic as epi8.
+template <typename T, int MODE>
+__device__ __forceinline__ uint4 epi_vec_pw(uint4 in, const uint32_t* acc8, float scale) {
+  const T* h = reinterpret_cast<const T*>(&in);
+  uint4 o;
+  T* oh = reinterpret_cast<T*>(&o);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ev[j] = St<T>::ld(ah[j]) - rnd<T>(acc[j]);
-    Vec8<T>::st(reinterpret_cast<T*>(p.out) + g * p.gs_out + idx, ev);
-  } else if constexpr (MODE == MODE_I) {
-    const T* xh = reinterpret_cast<const T*>(&xv);
-    float xn[8];
+  for (int j = 0; j < 8; ++j) {
+    const float a = __uint_as_float(acc8[j]);
+    if constexpr (MODE == MODE_P)
+      oh[j] = St<T>::st(St<T>::ld(h[j]) - rnd<T>(a));
+    else
+      oh[j] = St<T>::st(St<T>::ld(h[j]) + scale * a);
+  }
+  return o;
+}
+
+template <typename T, int ACT>
+__device__ __forceinline__ void epi_vec_i(uint4 ev, uint4& xv, uint4& av, const uint32_t* acc8, float gamma,
+                                          int from_stored) {
+  const T* eh = reinterpret_cast<const T*>(&ev);
+  T* xh = reinterpret_cast<T*>(&xv);
+  T* ah = reinterpret_cast<T*>(&av);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float x0 = St<T>::ld(xh[j]);
-      xn[j] = x0 + p.scale * (-St<T>::ld(ah[j]) + act_df_hw<ACT>(x0) * acc[j]);
-    }
-    Vec8<T>::st(reinterpret_cast<T*>(p.out) + g * p.gs_out + idx, xn);
-    if (p.aux2 != nullptr) {
-      float an[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) an[j] = act_f_hw<ACT>(p.a_out_from_stored ? rnd<T>(xn[j]) : xn[j]);
-      Vec8<T>::st(reinterpret_cast<T*>(p.aux2) + g * p.gs_aux2 + idx, an);
-    }
-  } else if constexpr (MODE == MODE_W) {
-    float wv[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) wv[j] = St<T>::ld(ah[j]) + p.scale * acc[j];
-    Vec8<T>::st(reinterpret_cast<T*>(p.out) + g * p.gs_out + idx, wv);
+  for (int j = 0; j < 8; ++j) {
+    const float x0 = St<T>::ld(xh[j]);
+    const float xn = x0 + gamma * (-St<T>::ld(eh[j]) + act_df_hw<ACT>(x0) * __uint_as_float(acc8[j]));
+    xh[j] = St<T>::st(xn);
+    ah[j] = St<T>::st(act_f_hw<ACT>(from_stored ? rnd<T>(xn) : xn));
   }
 }
 
-// I: one 32-column chunk of the row's E and X operands (4 vectors of 8).
-template <typename T>
-__device__ __forceinline__ void i_chunk_load(const TcParams& p, int g, int m, int n, uint4 (&ev)[4],
-                                             uint4 (&xv)[4]) {
-  if (m >= p.Mg) return;
-  const long long row = (long long)m * p.ld_out;
-#pragma unroll
-  for (int v = 0; v < 4; ++v) {
-    if (n + 8 * v < p.Ng) {
-      ev[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + row + n + 8 * v);
-      xv[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.out) + g * p.gs_out + row + n + 8 * v);
-    }
-  }
+// TMA loads of one I epilogue chunk into a slot: the E tile (map0) and the X tile (map1).
+__device__ __forceinline__ void epi_load_i(const CUtensorMap* map0, const CUtensorMap* map1, uint32_t slot,
+                                           uint32_t bar, uint32_t tile_bytes, int n, int r0, int g) {
+  mbar_expect_tx(bar, 2 * tile_bytes);
+  tma_load_3d(slot, map0, bar, n, r0, g);
+  tma_load_3d(slot + tile_bytes, map1, bar, n, r0, g);
 }
 
 template <typename T, int ACT, int MODE, int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ TcParams p) {
+                   const __grid_constant__ CUtensorMap tmE0, const __grid_constant__ CUtensorMap tmE1,
+                   const __grid_constant__ CUtensorMap tmE2, const __grid_constant__ TcParams p) {
+  // tmE0..2: the I epilogue's operand maps (E, X, A_out)
   constexpr bool A_MN = (MODE == MODE_I);
   constexpr bool B_MN = (MODE == MODE_P || MODE == MODE_I || MODE == MODE_F);
   constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
@@ -314,12 +347,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TC_STAGES * STAGE_BYTES);
-  // bars: full[S], empty[S], tfull[2], tempty[2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * TC_STAGES + 4);
+  constexpr bool EPI_STAGED = (MODE == MODE_P || MODE == MODE_W || MODE == MODE_I);
+  constexpr uint32_t EPI_REGION = EPI_STAGED ? EPI_BYTES : 0;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TC_STAGES * STAGE_BYTES + EPI_REGION);
+  // bars: full[S], empty[S], tfull[2], tempty[2], epilogue slots[2 per epilogue warp]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * TC_STAGES + 4 + 2 * TC_EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const uint32_t full0 = saddr(bars), empty0 = saddr(bars + TC_STAGES);
   const uint32_t tfull0 = saddr(bars + 2 * TC_STAGES), tempty0 = saddr(bars + 2 * TC_STAGES + 2);
+  const uint32_t ebar0 = saddr(bars + 2 * TC_STAGES + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -331,6 +367,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(tfull0 + 8 * b, 1);
       mbar_init(tempty0 + 8 * b, 32 * TC_EPI_WARPS);
     }
+    for (int b = 0; b < 2 * TC_EPI_WARPS; ++b) mbar_init(ebar0 + 8 * b, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -425,91 +462,197 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // ------------------------------- epilogue --------------------------------
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;     // TMEM lane quarter this warp may access
     constexpr int HC = BN / 2;  // accumulator columns per epilogue warp
     const int c_lo = ((warp - 2) >> 2) * HC;
     int acc = 0;
     uint32_t aphase = 0;
-    // P and W (one in/out stream, a light epilogue): the row's operand is loaded before the
-    // accumulator is ready, so its memory latency overlaps the tile's MMAs.  I (two input streams,
-    // f and f') keeps a rolled chunk loop that loads E and X one 32-column chunk ahead: unrolled, it
-    // would crowd the instruction cache the MMA issuer shares and spill.
-    constexpr int PF = (MODE == MODE_P || MODE == MODE_W) ? HC : 0;
-    constexpr int NPF = PF / 8 > 0 ? PF / 8 : 1;
-    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
-      int g, m0, n0, sp;
-      tile_coords(p, t, BN, g, m0, n0, sp);
-      const int m = m0 + 32 * q + lane;
-      uint4 pfa[NPF], pfx[MODE == MODE_I ? NPF : 1];
-      const bool pre = PF > 0 && p.splits == 1 && m < p.Mg;
-      if (pre) {
-        const long long row = (long long)m * p.ld_out;
+    bool staged = false;
+    if constexpr (EPI_STAGED) staged = p.staged != 0;
+    const bool xpose = (MODE == MODE_P || MODE == MODE_W) && staged;
+    if (xpose) {
+      {
+        // P / W: the warp's 32 x HC block of the in/out operand (X_lo or W) is read with coalesced
+        // 16-byte loads into registers while the tile's MMAs run (the next tile's block as soon as
+        // this one is in shared memory), then per 64-column chunk: registers -> swizzled shared
+        // buffer, each row thread applies the epilogue to its row in place, and the chunk leaves
+        // with coalesced 16-byte stores (a warp instruction covers 4 rows x 128 bytes).
+        constexpr int NCH = HC / 64;        // 64-column chunks per warp and tile
+        constexpr int NPRE = 8 * NCH;       // prefetched 16-byte vectors per thread
+        const uint32_t xb = saddr(smem + TC_STAGES * STAGE_BYTES) + (warp - 2) * EPI_WARP_BYTES;
+        const T* src = reinterpret_cast<const T*>(MODE == MODE_P ? p.aux : p.out);
+        const long long gsrc = MODE == MODE_P ? p.gs_aux : p.gs_out;
+        T* dst = reinterpret_cast<T*>(p.out);
+        const int cr = lane >> 3, cj = lane & 7;  // coalesced layout: row 4i + cr, vector cj
+        uint4 pre[NPRE];
+        auto prefetch = [&](int t) {
+          int g, m0, n0, sp;
+          tile_coords(p, t, BN, g, m0, n0, sp);
+          const int r0 = m0 + 32 * q, nw = n0 + c_lo;
 #pragma unroll
-        for (int v = 0; v < PF / 8; ++v) {
-          const int n = n0 + c_lo + 8 * v;
-          if (n < p.Ng) {
-            if constexpr (MODE == MODE_P)
-              pfa[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + row + n);
-            else if constexpr (MODE == MODE_W)
-              pfa[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.out) + g * p.gs_out + row + n);
-            else if constexpr (MODE == MODE_I) {
-              pfa[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + row + n);
-              pfx[v] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.out) + g * p.gs_out + row + n);
+          for (int cc = 0; cc < NCH; ++cc) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = r0 + 4 * i + cr, n = nw + 64 * cc + 8 * cj;
+              if (r < p.Mg && n < p.Ng)
+                pre[8 * cc + i] = *reinterpret_cast<const uint4*>(src + g * gsrc + (long long)r * p.ld_out + n);
             }
           }
+        };
+        if (blockIdx.x < p.tiles) prefetch(blockIdx.x);
+        for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
+          int g, m0, n0, sp;
+          tile_coords(p, t, BN, g, m0, n0, sp);
+          const int r0 = m0 + 32 * q, nw = n0 + c_lo;
+          const bool ok = mbar_wait(tfull0 + 8 * acc, aphase, abort_flag);
+          __syncwarp();
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t trow = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
+#pragma unroll
+          for (int cc = 0; cc < NCH; ++cc) {
+            // registers -> shared (row 4i + cr, vector cj; 128-byte rows, vector index ^ (row & 7))
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = 4 * i + cr;
+              sts128(xb + r * 128 + ((cj ^ (r & 7)) << 4), pre[8 * cc + i]);
+            }
+            if (cc == NCH - 1 && t + (int)gridDim.x < p.tiles) prefetch(t + gridDim.x);
+            __syncwarp();
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              uint32_t raw[32];
+              tmem_ld32(trow + c_lo + 64 * cc + 32 * hf, raw);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t a = xb + lane * 128 + (((4 * hf + j) ^ (lane & 7)) << 4);
+                sts128(a, epi_vec_pw<T, MODE>(lds128(a), raw + 8 * j, p.scale));
+              }
+            }
+            if (cc == NCH - 1) {  // every accumulator column read: release it to the MMA warp
+              tc_fence_before();
+              mbar_arrive(tempty0 + 8 * acc);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = 4 * i + cr, n = nw + 64 * cc + 8 * cj;
+              const uint4 v = lds128(xb + r * 128 + ((cj ^ (r & 7)) << 4));
+              if (r0 + r < p.Mg && n < p.Ng)
+                *reinterpret_cast<uint4*>(dst + g * p.gs_out + (long long)(r0 + r) * p.ld_out + n) = v;
+            }
+            __syncwarp();
+          }
+          if (++acc == 2) { acc = 0; aphase ^= 1; }
         }
       }
-      uint4 ce[4], cx[4];  // I: the current chunk's E and X, loaded one chunk ahead
-      if constexpr (MODE == MODE_I) i_chunk_load<T>(p, g, m, n0 + c_lo, ce, cx);
-      const bool ok = mbar_wait(tfull0 + 8 * acc, aphase, abort_flag);
-      __syncwarp();
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t trow = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
+    } else if (staged) {
       if constexpr (MODE == MODE_I) {
+        // I: E and X staged through shared memory in 16-column chunks (two 2 KB slots per warp).
+        // The first two chunks are requested with TMA before the accumulator is ready; chunk s + 2 as
+        // soon as chunk s's TMA stores (X, and A_out when given) have read its slot.
+        constexpr int CW = 16;
+        constexpr int NSUB = HC / CW;
+        constexpr uint32_t TILE = 32 * CW * 2;  // one 32-row operand tile (32-byte rows)
+        const uint32_t ebase = saddr(smem + TC_STAGES * STAGE_BYTES) + (warp - 2) * EPI_WARP_BYTES;
+        const uint32_t ebar = ebar0 + 16 * (warp - 2);
+        uint32_t eph = 0, pending = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+          int g, m0, n0, sp;
+          tile_coords(p, t, BN, g, m0, n0, sp);
+          const int r0 = m0 + 32 * q;
+          const bool live = r0 < p.Mg;
+          const int nw = n0 + c_lo;
+          if (live && lane == 0) {
+            bulk_wait_read0();  // the previous tile's stores have read both slots
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {
+              if (nw + CW * s < p.Ng) {
+                epi_load_i(&tmE0, &tmE1, ebase + s * EPI_SLOT, ebar + 8 * s, TILE, nw + CW * s, r0, g);
+                pending |= 1u << s;
+              }
+            }
+          }
+          __syncwarp();
+          if (!mbar_wait(tfull0 + 8 * acc, aphase, abort_flag)) ok = false;
+          __syncwarp();
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t trow = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
+#pragma unroll 1
+          for (int c = 0; c < HC / 32 && ok; ++c) {
+            uint32_t raw[32];
+            tmem_ld32(trow + c_lo + 32 * c, raw);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int sidx = 2 * c + h, slot = h;
+              const int n = nw + CW * sidx;
+              if (!live || n >= p.Ng || !ok) continue;
+              if (!mbar_wait(ebar + 8 * slot, (eph >> slot) & 1u, abort_flag)) {
+                ok = false;
+                continue;
+              }
+              eph ^= 1u << slot;
+              pending &= ~(1u << slot);
+              const uint32_t sb = ebase + slot * EPI_SLOT;
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {  // 32-byte rows, 32-byte swizzle: vector j ^ ((row >> 2) & 1)
+                const uint32_t off = lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
+                uint4 xv = lds128(sb + TILE + off), av;
+                epi_vec_i<T, ACT>(lds128(sb + off), xv, av, raw + 16 * h + 8 * j, p.scale, p.a_out_from_stored);
+                sts128(sb + TILE + off, xv);
+                if (p.aux2 != nullptr) sts128(sb + off, av);
+              }
+              fence_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_3d(&tmE1, sb + TILE, n, r0, g);
+                if (p.aux2 != nullptr) tma_store_3d(&tmE2, sb, n, r0, g);
+                bulk_commit();
+                if (sidx + 2 < NSUB && n + 2 * CW < p.Ng) {
+                  bulk_wait_read0();
+                  epi_load_i(&tmE0, &tmE1, sb, ebar + 8 * slot, TILE, n + 2 * CW, r0, g);
+                  pending |= 1u << slot;
+                }
+              }
+              __syncwarp();
+            }
+          }
+          if (!ok) break;
+          tc_fence_before();
+          mbar_arrive(tempty0 + 8 * acc);
+          if (++acc == 2) { acc = 0; aphase ^= 1; }
+        }
+        if (lane == 0) {
+          // loads still in flight (only after an aborted wait) land before the CTA exits
+#pragma unroll
+          for (int s = 0; s < 2; ++s)
+            if ((pending >> s) & 1u) mbar_drain(ebar + 8 * s, (eph >> s) & 1u);
+          bulk_wait0();
+        }
+        __syncwarp();
+      }
+    } else {
+      for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
+        int g, m0, n0, sp;
+        tile_coords(p, t, BN, g, m0, n0, sp);
+        const int m = m0 + 32 * q + lane;
+        const bool ok = mbar_wait(tfull0 + 8 * acc, aphase, abort_flag);
+        __syncwarp();
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t trow = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
 #pragma unroll 1
         for (int c = 0; c < HC / 32; ++c) {
           uint32_t raw[32];
           tmem_ld32(trow + c_lo + 32 * c, raw);
-          uint4 ne[4], nx[4];
-          if (c + 1 < HC / 32) i_chunk_load<T>(p, g, m, n0 + c_lo + 32 * (c + 1), ne, nx);
           if (m < p.Mg) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               const int n = n0 + c_lo + 32 * c + 8 * v;
-              if (n < p.Ng) {
-                float a8[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[8 * v + j]);
-                epi8_pre<T, ACT, MODE>(p, g, m, n, a8, ce[v], cx[v]);
-              }
-            }
-          }
-#pragma unroll
-          for (int v = 0; v < 4; ++v) { ce[v] = ne[v]; cx[v] = nx[v]; }
-        }
-        tc_fence_before();
-        mbar_arrive(tempty0 + 8 * acc);
-        if (++acc == 2) { acc = 0; aphase ^= 1; }
-        continue;
-      }
-#pragma unroll(PF > 0 ? HC / 32 : 1)
-      for (int c = 0; c < HC / 32; ++c) {
-        uint32_t raw[32];
-        tmem_ld32(trow + c_lo + 32 * c, raw);
-        if (m < p.Mg) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const int n = n0 + c_lo + 32 * c + 8 * v;
-            const int vi = 4 * c + v;  // vector index within the row
-            if (n < p.Ng) {
-              if (pre && vi < PF / 8) {
-                float a8[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[8 * v + j]);
-                epi8_pre<T, ACT, MODE>(p, g, m, n, a8, pfa[vi < NPF ? vi : 0],
-                                       pfx[MODE == MODE_I && vi < NPF ? vi : 0]);
-              } else if (p.splits > 1) {  // fp32 partial of this K range; the reduce pass applies the epilogue
+              if (n >= p.Ng) continue;
+              if (p.splits > 1) {  // fp32 partial of this K range; the reduce pass applies the epilogue
                 float4* dst = reinterpret_cast<float4*>(
                     p.ws + (((long long)sp * p.groups + g) * p.Mg + m) * (long long)p.Ng + n);
                 dst[0] = make_float4(__uint_as_float(raw[8 * v]), __uint_as_float(raw[8 * v + 1]),
@@ -525,10 +668,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
           }
         }
+        tc_fence_before();
+        mbar_arrive(tempty0 + 8 * acc);
+        if (++acc == 2) { acc = 0; aphase ^= 1; }
       }
-      tc_fence_before();
-      mbar_arrive(tempty0 + 8 * acc);
-      if (++acc == 2) { acc = 0; aphase ^= 1; }
     }
   }
   tc_fence_before();
@@ -555,7 +698,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 3-D map over a [groups][rows][inner] row-major array (element strides ld, gs).
 int make_map(CUtensorMap* map, const void* base, int dtype, long long inner, long long rows, long long groups,
-             long long ld, long long gs, int box_inner, int box_rows) {
+             long long ld, long long gs, int box_inner, int box_rows,
+             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (fn == nullptr) return set_error(IPC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)groups};
@@ -564,7 +708,7 @@ int make_map(CUtensorMap* map, const void* base, int dtype, long long inner, lon
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUtensorMapDataType dt = dtype == IPC_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(IPC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return IPC_OK;
 }
@@ -643,7 +787,7 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   if ((MODE == MODE_W || MODE == MODE_WD) && ws != nullptr && p.tiles < num_sms() / 2 && nk >= 8 &&
       a.gsOut == (long long)a.Mg * a.Ng) {  // the reduce pass walks out as one dense [groups][M][N] array
     const long long tile_bytes = (long long)a.groups * a.Mg * a.Ng * 4;
-    int splits = (num_sms() + p.tiles - 1) / p.tiles;
+    int splits = num_sms() / p.tiles;  // one wave: every (tile, split) unit resident at once
     splits = min(splits, nk / 4);
     const long long fit = (long long)(ws_bytes / (size_t)tile_bytes);
     if (fit < splits) splits = (int)fit;
@@ -654,13 +798,28 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
     }
   }
   p.tiles *= p.splits;
+  // staged epilogue (no split-K): P / W through the transpose buffer, I through TMA with three maps
+  // (E, X, A_out) of 32-row x 16-column boxes, 32-byte swizzle
+  constexpr bool EPI_STAGED = (MODE == MODE_P || MODE == MODE_W || MODE == MODE_I);
+  CUtensorMap te[3];
+  memset(te, 0, sizeof(te));
+  p.staged = EPI_STAGED && p.splits == 1;
+  if (MODE == MODE_I && p.staged) {
+    const void* src[3] = {a.aux, a.out, a.aux2};
+    const long long gs[3] = {a.gsAux, a.gsOut, a.gsAux2};
+    for (int i = 0; i < 3; ++i) {
+      if (src[i] == nullptr) continue;
+      rc = make_map(&te[i], src[i], dtype, a.Ng, a.Mg, a.groups, a.Ng, gs[i], 16, 32, CU_TENSOR_MAP_SWIZZLE_32B);
+      if (rc) return rc;
+    }
+  }
   constexpr int STAGE_BYTES = (TC_BM + BN) * TC_BK * 2;
-  const int smem = TC_STAGES * STAGE_BYTES + 1024 + 256;
+  const int smem = TC_STAGES * STAGE_BYTES + (EPI_STAGED ? EPI_BYTES : 0) + 1024 + 256;
   auto kern = tc_gemm_kernel<T, ACT, MODE, BN>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "tcgen05 kernel smem attribute: %s", cudaGetErrorString(err));
   const int grid = p.tiles < num_sms() ? p.tiles : num_sms();
-  kern<<<grid, TC_THREADS, smem, s>>>(ta, tb, p);
+  kern<<<grid, TC_THREADS, smem, s>>>(ta, tb, te[0], te[1], te[2], p);
   count_launch();
   int rc2 = check_launch("tcgen05 GEMM");
   if (rc2 || p.splits == 1) return rc2;
@@ -721,9 +880,20 @@ bool tc_eligible(int mode, int M, int K, int B, int dtype, int algo, bool b_acti
 int launch_tc(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes) {
   if (a.Mg <= 0 || a.Ng <= 0 || a.groups <= 0) return IPC_OK;
   if (a.Kg <= 0) return launch_generic(a, mode, false, act, dtype, s);  // nothing to multiply
-  // 128 x 256 tiles unless that leaves SMs idle and 128 x 128 tiles would not
+  // TMA maps and 16-byte epilogue vectors need 16-byte aligned operands; a view that starts mid-vector
+  // takes the generic kernel
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.Bm) |
+                        reinterpret_cast<uintptr_t>(a.out) | reinterpret_cast<uintptr_t>(a.aux) |
+                        reinterpret_cast<uintptr_t>(a.aux2);
+  if (mis & 15) return launch_generic(a, mode, false, act, dtype, s);
+  // 128 x 256 tiles unless that leaves SMs idle and 128 x 128 tiles would not.  A weight update that
+  // splits its batch reduction (split-K) fills the SMs with splits instead, and the wider tile reads
+  // a third less operand data from L2 per FLOP.
   const long long t256 = (long long)((a.Mg + TC_BM - 1) / TC_BM) * ((a.Ng + 255) / 256) * a.groups;
-  const bool wide = a.Ng >= 256 && t256 >= num_sms();
+  const bool splitk = (mode == MODE_W || mode == MODE_WD) && ws != nullptr && t256 < num_sms() / 2 &&
+                      (a.Kg + TC_BK - 1) / TC_BK >= 8 && a.gsOut == (long long)a.Mg * a.Ng &&
+                      ws_bytes >= (size_t)(2LL * a.groups * a.Mg * a.Ng * 4);
+  const bool wide = a.Ng >= 256 && (t256 >= num_sms() || splitk);
   if (dtype == IPC_DT_F16)
     return wide ? dispatch_mode<__half, 256>(a, mode, act, dtype, s, ws, ws_bytes)
                 : dispatch_mode<__half, 128>(a, mode, act, dtype, s, ws, ws_bytes);

@@ -3,8 +3,9 @@
 Every mode against the CPU oracle (storage rounding of the reference kernels,
 float64 accumulation), bound ``max|got - ref| / max|ref| <= 1e-2`` (the 16-bit
 gate); the fp32 weight delta ``<= 1e-3``.  Also: tails in M / N / K (TMA zero
-fill + epilogue masks), grouped launches, agreement with the mma.sync kernel
-(two storage rounding steps),
+fill + TMA store clipping + epilogue masks), grouped launches, agreement with
+the mma.sync kernel (two storage rounding steps), the staged I epilogue without
+an A_out operand, operands that start mid-vector (routed to the generic kernel),
 and a clean device status word (no bounded wait expired).
 """
 import pytest
@@ -137,3 +138,46 @@ def test_tcgen05_rejects_activated_operand_and_bad_strides():
     # auto falls back to the generic kernel for the same request
     N.fused_gemm(N.MODE_PRED, x, x, x, x, M=256, K=256, B=256, flags=N.FLAG_ACTIVATE_B, act="tanh")
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("mode_name", ["PRED", "INFER", "WEIGHT"])
+def test_misaligned_views_take_the_generic_kernel(mode_name):
+    """Operands that start 8 bytes into an allocation cannot be TMA-mapped: auto routes them to the
+    generic kernel, which gives the oracle's answer."""
+    N = _N()
+    mode = getattr(N, f"MODE_{mode_name}")
+    M = K = B = 256
+    dt = torch.float16
+    ins, _, scale = _run(mode, M, K, B, dt, "tcgen05", seed=21)
+    dev = {}
+    for k, v in ins.items():
+        buf = torch.zeros(v.numel() + 4, dtype=v.dtype, device=DEV)
+        view = buf[4:].view(v.shape)
+        view.copy_(v.to(DEV))
+        assert view.data_ptr() % 16 == 8
+        dev[k] = view
+    N.fused_gemm(mode, dev["a"], dev["b"], dev["out"], dev.get("aux"), dev.get("aux2"), M=M, K=K, B=B,
+                 scale=scale, flags=N.FLAG_AOUT_STORED if mode == N.MODE_INFER else 0, act="tanh", dtype=dt)
+    torch.cuda.synchronize()
+    assert N.device_status() == 0
+    ref, ref_a = _ref(mode, ins, dt, scale)
+    assert O.rel_inf(dev["out"].cpu(), ref) <= 1e-2
+    if ref_a is not None:
+        assert O.rel_inf(dev["aux2"].cpu(), ref_a) <= 1e-2
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_infer_without_activation_output(dt):
+    """The staged I epilogue with no A_out operand writes X only."""
+    N = _N()
+    M, K, B = 384, 1024, 264
+    ins = dict(a=_r((K, M), 31, M ** -0.5, dt), b=_r((K, B), 32, 0.5, dt), aux=_r((M, B), 33, 0.5, dt),
+               out=_r((M, B), 34, 1, dt))
+    dev = {k: v.to(DEV) for k, v in ins.items()}
+    N.fused_gemm(N.MODE_INFER, dev["a"], dev["b"], dev["out"], dev["aux"], None, M=M, K=K, B=B, scale=0.5,
+                 act="tanh", dtype=dt, algo="tcgen05")
+    torch.cuda.synchronize()
+    assert N.device_status() == 0
+    ref, _ = _ref(N.MODE_INFER, ins, dt, 0.5)
+    assert O.rel_inf(dev["out"].cpu(), ref) <= 1e-2
+    assert torch.equal(dev["aux"].cpu(), ins["aux"])  # E is read, never written
