@@ -564,17 +564,28 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
       // P: e[l] = cast(x[l]) - cast(W[l] f(x[l+1])), l < L-1 on tensor cores; the input layer uses mu
       {
         int base = 0;
-        for (int l = 0; l < Lt; ++l) {
+#pragma unroll
+        for (int l = 0; l < MAXL; ++l) {  // unrolled: the per-layer offsets become constant-bank operands
+          if (l >= Lt) break;
           const int mtiles = p.rows16[l] / 16, ksteps = p.rows16[l + 1] / 16, units = mtiles * NT;
           for (int u = (warp - base % NET_WARPS + NET_WARPS) % NET_WARPS; u < units; u += NET_WARPS) {
             const int mt = u / NT, nt = u % NT;
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int ks = 0; ks < ksteps; ++ks) {
-              uint32_t af[4], bf[2];
-              frag_a(af, sbase + p.o_w[l], WLD, mt * 16, ks * 16, lane);
-              frag_b_sw<NCOL>(bf, sbase + p.o_a[l + 1], ks * 16, nt * 8, lane);
-              mma<T>(acc, af, bf[0], bf[1]);
-            }
+            // all fragments first, then two accumulator chains (even / odd k steps): the legacy
+            // mma.sync latency, not its throughput, bounds these reductions of at most 4 steps
+            // (every width the kernel accepts is <= 64, checked at launch)
+            float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t af[4][4], bf[4][2];
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              if (ks < ksteps) {
+                frag_a(af[ks], sbase + p.o_w[l], WLD, mt * 16, ks * 16, lane);
+                frag_b_sw<NCOL>(bf[ks], sbase + p.o_a[l + 1], ks * 16, nt * 8, lane);
+              }
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              if (ks < ksteps) mma<T>((ks & 1) ? acc2 : acc, af[ks], bf[ks][0], bf[ks][1]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[j] += acc2[j];
             const int c = nt * 8 + 2 * tq;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -596,17 +607,25 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
       // I: x[l] += g(-e[l] + f'(x[l]) (W[l-1]^T e[l-1])), l = 1..L-1
       {
         int base = 0;
-        for (int l = 1; l <= Lt; ++l) {
+#pragma unroll
+        for (int l = 1; l <= MAXL; ++l) {
+          if (l > Lt) break;
           const int mtiles = p.rows16[l] / 16, ksteps = p.rows16[l - 1] / 16, units = mtiles * NT;
           for (int u = (warp - base % NET_WARPS + NET_WARPS) % NET_WARPS; u < units; u += NET_WARPS) {
             const int mt = u / NT, nt = u % NT;
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int ks = 0; ks < ksteps; ++ks) {
-              uint32_t af[4], bf[2];
-              frag_a_t(af, sbase + p.o_w[l - 1], WLD, mt * 16, ks * 16, lane);
-              frag_b_sw<NCOL>(bf, sbase + p.o_e[l - 1], ks * 16, nt * 8, lane);
-              mma<T>(acc, af, bf[0], bf[1]);
-            }
+            float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t af[4][4], bf[4][2];
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              if (ks < ksteps) {
+                frag_a_t(af[ks], sbase + p.o_w[l - 1], WLD, mt * 16, ks * 16, lane);
+                frag_b_sw<NCOL>(bf[ks], sbase + p.o_e[l - 1], ks * 16, nt * 8, lane);
+              }
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              if (ks < ksteps) mma<T>((ks & 1) ? acc2 : acc, af[ks], bf[ks][0], bf[ks][1]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[j] += acc2[j];
             const int c = nt * 8 + 2 * tq;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
