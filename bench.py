@@ -399,7 +399,8 @@ def run_c5(args, world, rank, local):
         raise SystemExit(f"global batch {Bg} must split into multiples of 8 over {world} ranks")
     B = Bg // world
     cfg = IPCConfig(dims=dims, alpha=1e-4, gamma=0.5, activation="tanh", dtype=dtype)
-    dp = DataParallelIPC(cfg, device=dev)
+    dp = DataParallelIPC(cfg, device=dev) if args.comm_sms < 0 else DataParallelIPC(cfg, device=dev,
+                                                                                     comm_sms=args.comm_sms)
     w_init = [w.to(dev, dtype) for w in S.fan_in_normal(dims, seed=1)]
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     pool = []
@@ -489,6 +490,7 @@ def run_c5(args, world, rank, local):
         "config": {"workload": "configs[4] wide batch-sharded: dims (1000,4096x6,4096), global batch 65536, T=4, "
                                "tanh, bf16 storage / fp32 accumulation, per-layer fp32 dW all-reduce (NCCL)",
                    "global_batch": Bg, "batch_per_rank": B, "T": T, "parallelism": f"dp{world}",
+                   "comm_sms": dp.comm_sms if world > 1 else 0,
                    "l2": "inputs larger than L2 (the per-step state is GBs)"},
         "roofline": roof,
         "e2e": {"value": round(n_e2e * Bg / (ms_e2e * 1e-3), 1), "unit": "samples/s",
@@ -1043,6 +1045,8 @@ def main():
     ap.add_argument("--depth", type=int, default=6)
     ap.add_argument("--act", default="tanh")
     ap.add_argument("--chunk", type=int, default=500, help="training steps per persistent-kernel launch")
+    ap.add_argument("--comm-sms", type=int, default=-1,
+                    help="c5: SMs the delta GEMMs leave to the overlapped all-reduces (default: DataParallelIPC's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

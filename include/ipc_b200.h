@@ -218,6 +218,15 @@ int ipc_device_status(int* status, int clear);
  * IPC_NET_SYNC_BYTES of device memory.  No reference counterpart. */
 int ipc_selftest_barrier_timeout(void* sync, int limit_us, void* stream);
 
+/* Cap on the CTAs of the persistent tensor-core GEMM (max_ctas = 0: one per
+ * SM, the default).  Its CTAs otherwise fill every SM, so a collective
+ * launched beside it (the data-parallel path's NCCL all-reduce of the weight
+ * deltas, issued while later layers' deltas are still being formed) waits for
+ * them; with SMs left over the two run concurrently.  Process-wide, read when
+ * a GEMM is launched; IPC_ERR_ARG for max_ctas < 0.  No reference
+ * counterpart. */
+int ipc_set_max_ctas(int max_ctas);
+
 /* A = cast(f(X)) over n elements (materialise a saved activation). */
 int ipc_activate(void* a, const void* x, long long n, int act, int dtype, void* stream);
 

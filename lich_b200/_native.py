@@ -45,7 +45,7 @@ EXPORTED = (
     "ipc_abi_version", "ipc_last_error", "ipc_launch_count", "ipc_pred_err", "ipc_pred_err_saved",
     "ipc_forward", "ipc_infer_update", "ipc_weight_update", "ipc_weight_delta", "ipc_weight_apply",
     "ipc_activate", "ipc_net_train", "ipc_net_plan", "ipc_fused_gemm", "ipc_device_status",
-    "ipc_fused_gemm_ws", "ipc_weight_update_noalloc", "ipc_selftest_barrier_timeout",
+    "ipc_fused_gemm_ws", "ipc_weight_update_noalloc", "ipc_selftest_barrier_timeout", "ipc_set_max_ctas",
 )
 
 
@@ -124,6 +124,7 @@ def load() -> ctypes.CDLL:
         "ipc_fused_gemm_ws": (i, [i, vp, vp, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp, c_size_t, vp]),
         "ipc_weight_update_noalloc": (i, [i, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp]),
         "ipc_selftest_barrier_timeout": (i, [vp, i, vp]),
+        "ipc_set_max_ctas": (i, [i]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -211,6 +212,11 @@ def device_status(clear: bool = True) -> int:
     v = c_int(0)
     check(load().ipc_device_status(ctypes.byref(v), int(clear)))
     return v.value
+
+
+def set_max_ctas(max_ctas: int) -> None:
+    """Cap the CTAs of persistent tensor-core GEMMs (0 = one per SM); see ``ipc_set_max_ctas``."""
+    check(load().ipc_set_max_ctas(int(max_ctas)))
 
 
 def launch_count() -> int:

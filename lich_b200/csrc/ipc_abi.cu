@@ -260,6 +260,8 @@ int ipc_fused_gemm_ws(int mode, const void* a, const void* b, void* out, const v
                          static_cast<float*>(workspace), workspace_bytes, stream);
 }
 
+int ipc_set_max_ctas(int max_ctas) { return set_max_ctas(max_ctas); }
+
 int ipc_selftest_barrier_timeout(void* sync, int limit_us, void* stream) {
   int rc = require_sm100();
   if (rc) return rc;

@@ -40,6 +40,7 @@
 // reads the word).
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -713,6 +714,8 @@ int make_map(CUtensorMap* map, const void* base, int dtype, long long inner, lon
   return IPC_OK;
 }
 
+std::atomic<int> g_max_ctas{0};  // ipc_set_max_ctas: 0 = one persistent CTA per SM
+
 int num_sms() {
   static int n[64] = {0};
   int dev = 0;
@@ -720,6 +723,12 @@ int num_sms() {
   if (dev < 0 || dev >= 64) return 148;
   if (n[dev] == 0) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
   return n[dev] > 0 ? n[dev] : 148;
+}
+
+// CTAs a persistent launch may use: every SM, or fewer while a caller leaves SMs to a collective.
+int grid_cap() {
+  const int n = num_sms(), c = g_max_ctas.load(std::memory_order_relaxed);
+  return (c > 0 && c < n) ? c : n;
 }
 
 // Split-K second pass: out = epilogue(sum over splits of the fp32 partials), summed in split order
@@ -784,10 +793,11 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   p.splits = 1;
   p.kps = nk;
   p.ws = nullptr;
-  if ((MODE == MODE_W || MODE == MODE_WD) && ws != nullptr && p.tiles < num_sms() / 2 && nk >= 8 &&
+  const int cap = grid_cap();
+  if ((MODE == MODE_W || MODE == MODE_WD) && ws != nullptr && p.tiles < cap / 2 && nk >= 8 &&
       a.gsOut == (long long)a.Mg * a.Ng) {  // the reduce pass walks out as one dense [groups][M][N] array
     const long long tile_bytes = (long long)a.groups * a.Mg * a.Ng * 4;
-    int splits = num_sms() / p.tiles;  // one wave: every (tile, split) unit resident at once
+    int splits = cap / p.tiles;  // one wave: every (tile, split) unit resident at once
     splits = min(splits, nk / 4);
     const long long fit = (long long)(ws_bytes / (size_t)tile_bytes);
     if (fit < splits) splits = (int)fit;
@@ -818,7 +828,7 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   auto kern = tc_gemm_kernel<T, ACT, MODE, BN>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "tcgen05 kernel smem attribute: %s", cudaGetErrorString(err));
-  const int grid = p.tiles < num_sms() ? p.tiles : num_sms();
+  const int grid = p.tiles < cap ? p.tiles : cap;
   kern<<<grid, TC_THREADS, smem, s>>>(ta, tb, te[0], te[1], te[2], p);
   count_launch();
   int rc2 = check_launch("tcgen05 GEMM");
@@ -890,15 +900,21 @@ int launch_tc(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, f
   // splits its batch reduction (split-K) fills the SMs with splits instead, and the wider tile reads
   // a third less operand data from L2 per FLOP.
   const long long t256 = (long long)((a.Mg + TC_BM - 1) / TC_BM) * ((a.Ng + 255) / 256) * a.groups;
-  const bool splitk = (mode == MODE_W || mode == MODE_WD) && ws != nullptr && t256 < num_sms() / 2 &&
+  const bool splitk = (mode == MODE_W || mode == MODE_WD) && ws != nullptr && t256 < grid_cap() / 2 &&
                       (a.Kg + TC_BK - 1) / TC_BK >= 8 && a.gsOut == (long long)a.Mg * a.Ng &&
                       ws_bytes >= (size_t)(2LL * a.groups * a.Mg * a.Ng * 4);
-  const bool wide = a.Ng >= 256 && (t256 >= num_sms() || splitk);
+  const bool wide = a.Ng >= 256 && (t256 >= grid_cap() || splitk);
   if (dtype == IPC_DT_F16)
     return wide ? dispatch_mode<__half, 256>(a, mode, act, dtype, s, ws, ws_bytes)
                 : dispatch_mode<__half, 128>(a, mode, act, dtype, s, ws, ws_bytes);
   return wide ? dispatch_mode<__nv_bfloat16, 256>(a, mode, act, dtype, s, ws, ws_bytes)
               : dispatch_mode<__nv_bfloat16, 128>(a, mode, act, dtype, s, ws, ws_bytes);
+}
+
+int set_max_ctas(int max_ctas) {
+  if (max_ctas < 0) return set_error(IPC_ERR_ARG, "max_ctas must be >= 0 (got %d)", max_ctas);
+  g_max_ctas.store(max_ctas, std::memory_order_relaxed);
+  return IPC_OK;
 }
 
 int read_device_status(int* status, int clear) {

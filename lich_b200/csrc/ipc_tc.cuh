@@ -12,6 +12,8 @@ bool tc_eligible(int mode, int M, int K, int B, int dtype, int algo, bool b_acti
 // ws / ws_bytes: optional fp32 workspace for split-K partial tiles (weight modes).
 int launch_tc(const GemmArgs& p, int mode, int act, int dtype, cudaStream_t s, float* ws = nullptr,
               size_t ws_bytes = 0);
+// Cap on the CTAs of a persistent tensor-core launch (0 = one per SM); see ipc_set_max_ctas.
+int set_max_ctas(int max_ctas);
 // Device status word written by bounded waits (0 = fine); clear != 0 resets it.
 int read_device_status(int* status, int clear);
 // The same for the bounded grid barriers of the wide small-batch step kernel (ipc_widenet.cu).

@@ -12,7 +12,11 @@ Each rank forms its fp32 partial ``dW_r[l]`` (``ipc_weight_delta`` /
 with one all-reduce per layer (issued as soon as that layer's partial is
 ready, so the reductions of earlier layers overlap the GEMMs of later ones),
 and every rank applies the same sum (``ipc_weight_apply``), keeping the
-replicas identical.  The reference is single-GPU; this is the scaling path of
+replicas identical.  While reductions are in flight the persistent GEMMs
+leave ``comm_sms`` SMs free (``ipc_set_max_ctas``): with every SM taken by a
+GEMM CTA, the collective's kernels would wait for the GEMM and the overlap
+would be lost.  Each layer's sum is applied as soon as its own reduction is
+done.  The reference is single-GPU; this is the scaling path of
 the wide configuration (batch 65536 over 1/2/4/8 B200s).
 """
 from __future__ import annotations
@@ -42,8 +46,12 @@ class DataParallelIPC:
     """Replicated weights, batch shards, one fp32 dW all-reduce per layer per training step."""
 
     def __init__(self, cfg: IPCConfig, *, device: torch.device, group=None, seed: int = 0,
-                 model: TileLangIPC | None = None):
+                 model: TileLangIPC | None = None, comm_sms: int = 24):
+        """comm_sms: SMs the delta GEMMs leave to the all-reduces they overlap (world > 1)."""
+        if comm_sms < 0:
+            raise ValueError("comm_sms must be >= 0")
         self.group = group
+        self.comm_sms = int(comm_sms)
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
         self.model = model if model is not None else TileLangIPC(cfg, device=device, seed=seed)
@@ -77,6 +85,14 @@ class DataParallelIPC:
             N.fused_gemm(N.MODE_WDELTA, m.e[l], m.x[l + 1], dw, M=d[l], K=d[l + 1], B=B, scale=self.cfg.alpha,
                          flags=N.FLAG_ACTIVATE_B, act=self.cfg.activation, dtype=self.cfg.dtype, device=m.device)
 
+    def _cap(self, leave: int) -> None:
+        """Leave `leave` SMs free of persistent GEMM CTAs (0 lifts the cap)."""
+        if leave <= 0:
+            N.set_max_ctas(0)
+            return
+        sms = torch.cuda.get_device_properties(self.model.w[0].device).multi_processor_count
+        N.set_max_ctas(max(1, sms - leave))
+
     def _apply(self, l: int, dw: torch.Tensor) -> None:
         w = self.model.w[l]
         N.check(N.load().ipc_weight_apply(w.data_ptr(), dw.data_ptr(), w.numel(), N.dtype_code(w.dtype),
@@ -94,13 +110,23 @@ class DataParallelIPC:
             m.step_initialized(update_weights=False)
         L = len(self.cfg.dims) - 1
         order = sorted(range(L), key=lambda l: -self._dw[l].numel())  # biggest reductions start first
-        handles = []
+        handles = {}
+        capped = False
+        try:
+            for l in order:
+                self._delta(l, self._dw[l])
+                hs = allreduce_deltas([self._dw[l]], self.group, async_op=True)
+                if hs:
+                    handles[l] = hs[0]
+                    if not capped and self.comm_sms > 0:
+                        self._cap(self.comm_sms)
+                        capped = True
+        finally:
+            if capped:
+                self._cap(0)
         for l in order:
-            self._delta(l, self._dw[l])
-            handles += allreduce_deltas([self._dw[l]], self.group, async_op=True)
-        for h in handles:
-            h.wait()
-        for l in order:
+            if l in handles:
+                handles[l].wait()
             self._apply(l, self._dw[l])
         m.steps_done += 1
 

@@ -63,13 +63,19 @@ def _worker(rank, world, port, data, out):
 
             def _apply(self, l, dw):
                 self.model.w[l] += dw
+                caps.append(("apply", l))
+
+            def _cap(self, leave):
+                caps.append(("cap", leave))
+
+        caps = []
 
         w0, x, y = data
         cols = slice(rank * B // world, (rank + 1) * B // world)
         model = _OracleModel(w0 if rank == 0 else [torch.zeros_like(t) for t in w0])  # rank 0 broadcasts
         dp = _DP(_Cfg(), device=torch.device("cpu"), model=model)
         dp.train_step(x[:, cols].contiguous(), y[:, cols].contiguous(), T=T)
-        out[rank] = ([t.clone() for t in dp.model.w], [t.clone() for t in dp.model.x])
+        out[rank] = ([t.clone() for t in dp.model.w], [t.clone() for t in dp.model.x], caps)
     finally:
         dist.destroy_process_group()
 
@@ -94,7 +100,11 @@ def test_sharded_step_equals_full_batch_step():
         res = dict(out)
     x_ref, w_ref, _, _ = O.train_step(x, y, w0, act=ACT, alpha=ALPHA, gamma=GAMMA, T=T)
     for rank in range(2):
-        w_got, x_got = res[rank]
+        w_got, x_got, caps = res[rank]
+        # the delta GEMMs after the first all-reduce leave SMs to it; the cap is lifted before the
+        # applies, and every layer is applied once
+        assert caps[0] == ("cap", 24) and caps[1] == ("cap", 0), caps
+        assert sorted(l for k, l in caps[2:] if k == "apply") == list(range(len(w0))), caps
         for l in range(len(w_ref)):
             assert O.rel_inf(w_got[l], w_ref[l]) <= 1e-5, (rank, "w", l)
         cols = slice(rank * B // 2, (rank + 1) * B // 2)

@@ -181,3 +181,19 @@ def test_infer_without_activation_output(dt):
     ref, _ = _ref(N.MODE_INFER, ins, dt, 0.5)
     assert O.rel_inf(dev["out"].cpu(), ref) <= 1e-2
     assert torch.equal(dev["aux"].cpu(), ins["aux"])  # E is read, never written
+
+
+def test_cta_cap_keeps_results():
+    """A GEMM launched with fewer persistent CTAs than SMs (ipc_set_max_ctas) gives the same answer."""
+    N = _N()
+    try:
+        for cap in (16, 1):
+            N.set_max_ctas(cap)
+            for mode in (N.MODE_PRED, N.MODE_WDELTA):
+                ins, got, scale = _run(mode, 512, 768, 384, torch.float16, "tcgen05", seed=41)
+                ref, _ = _ref(mode, ins, torch.float16, scale)
+                assert O.rel_inf(got["out"], ref) <= (1e-3 if mode == N.MODE_WDELTA else 1e-2), (cap, mode)
+    finally:
+        N.set_max_ctas(0)
+    with pytest.raises(N.IpcError):
+        N.set_max_ctas(-1)
