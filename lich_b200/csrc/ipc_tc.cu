@@ -216,12 +216,6 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes,
 
 template <typename T>
 struct Vec8 {
-  static __device__ __forceinline__ void ld(const T* p, float (&v)[8]) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(p);
-    const T* h = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = St<T>::ld(h[j]);
-  }
   static __device__ __forceinline__ void st(T* p, const float (&v)[8]) {
     uint4 raw;
     T* h = reinterpret_cast<T*>(&raw);
@@ -231,39 +225,13 @@ struct Vec8 {
   }
 };
 
-// Fused epilogue for 8 consecutive columns [n, n+8) of output row m.  f and f' use the MUFU forms
-// (relative error near 2^-11, one fp16 rounding step): every result here is stored in 16 bits.
+// Direct epilogue for 8 consecutive columns [n, n+8) of output row m, used by the modes without a
+// staged epilogue: WD (dw = alpha acc, or += with accumulate, fp32) and F (OUT = cast(acc) and
+// f(OUT), f in its MUFU form: one fp16 rounding step, every result is stored in 16 bits).
 template <typename T, int ACT, int MODE>
 __device__ __forceinline__ void epi8(const TcParams& p, int g, int m, int n, const float (&acc)[8]) {
   const long long idx = (long long)m * p.ld_out + n;
-  if constexpr (MODE == MODE_P) {
-    float xl[8], ev[8];
-    Vec8<T>::ld(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + idx, xl);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ev[j] = xl[j] - rnd<T>(acc[j]);
-    Vec8<T>::st(reinterpret_cast<T*>(p.out) + g * p.gs_out + idx, ev);
-  } else if constexpr (MODE == MODE_I) {
-    float xv[8], ev[8], xn[8];
-    T* xp = reinterpret_cast<T*>(p.out) + g * p.gs_out + idx;
-    Vec8<T>::ld(xp, xv);
-    Vec8<T>::ld(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + idx, ev);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) xn[j] = xv[j] + p.scale * (-ev[j] + act_df_hw<ACT>(xv[j]) * acc[j]);
-    Vec8<T>::st(xp, xn);
-    if (p.aux2 != nullptr) {
-      float an[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) an[j] = act_f_hw<ACT>(p.a_out_from_stored ? rnd<T>(xn[j]) : xn[j]);
-      Vec8<T>::st(reinterpret_cast<T*>(p.aux2) + g * p.gs_aux2 + idx, an);
-    }
-  } else if constexpr (MODE == MODE_W) {
-    float wv[8];
-    T* wp = reinterpret_cast<T*>(p.out) + g * p.gs_out + idx;
-    Vec8<T>::ld(wp, wv);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) wv[j] += p.scale * acc[j];
-    Vec8<T>::st(wp, wv);
-  } else if constexpr (MODE == MODE_WD) {
+  if constexpr (MODE == MODE_WD) {
     float4* dw = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + g * p.gs_out + idx);
     float4 a = make_float4(p.scale * acc[0], p.scale * acc[1], p.scale * acc[2], p.scale * acc[3]);
     float4 b = make_float4(p.scale * acc[4], p.scale * acc[5], p.scale * acc[6], p.scale * acc[7]);
@@ -274,7 +242,7 @@ __device__ __forceinline__ void epi8(const TcParams& p, int g, int m, int n, con
     }
     dw[0] = a;
     dw[1] = b;
-  } else {  // MODE_F
+  } else if constexpr (MODE == MODE_F) {
     float o[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = acc[j];
@@ -288,8 +256,9 @@ __device__ __forceinline__ void epi8(const TcParams& p, int g, int m, int n, con
   }
 }
 
-// The staged epilogue on one 16-byte vector (8 columns) of a thread's row: P e = x - cast(acc),
-// W w + alpha acc; I x + gamma (-e + f'(x) acc) and its activation.  Same arithmetic as epi8.
+// The staged epilogue on one 16-byte vector (8 columns) of a thread's row: P e = cast(x - cast(acc)),
+// W cast(w + alpha acc); I x_new = cast(x + gamma (-e + f'(x) acc)) and A_out = cast(f(x_new)) (of
+// cast(x_new) with a_out_from_stored), f and f' in their MUFU forms.
 template <typename T, int MODE>
 __device__ __forceinline__ uint4 epi_vec_pw(uint4 in, const uint32_t* acc8, float scale) {
   const T* h = reinterpret_cast<const T*>(&in);
@@ -664,7 +633,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 float a8[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[8 * v + j]);
-                epi8<T, ACT, MODE>(p, g, m, n, a8);
+                epi8<T, ACT, MODE>(p, g, m, n, a8);  // F, WD (P / I / W are staged)
               }
             }
           }
