@@ -385,7 +385,8 @@ C5_BATCH = 65536
 
 def run_c5(args, world, rank, local):
     """wide batch-sharded iPC -- dims (1000, 4096 x 6, 4096), global batch 65536 split over the
-    ranks, bf16, tanh, T=4; one fp32 dW all-reduce per layer per step (DataParallelIPC)."""
+    ranks, bf16, tanh, T=4; one fp32 dW reduction per layer per step (DataParallelIPC: reduce-scatter,
+    sliced apply, bf16 all-gather by default; --dp-reduce allreduce for the plain all-reduce)."""
     from lich_b200 import _native as N
     from lich_b200 import synthetic as S
     from lich_b200.data_parallel import DataParallelIPC
@@ -399,8 +400,10 @@ def run_c5(args, world, rank, local):
         raise SystemExit(f"global batch {Bg} must split into multiples of 8 over {world} ranks")
     B = Bg // world
     cfg = IPCConfig(dims=dims, alpha=1e-4, gamma=0.5, activation="tanh", dtype=dtype)
-    dp = DataParallelIPC(cfg, device=dev) if args.comm_sms < 0 else DataParallelIPC(cfg, device=dev,
-                                                                                     comm_sms=args.comm_sms)
+    dp_kw = {"reduce": args.dp_reduce}
+    if args.comm_sms >= 0:
+        dp_kw["comm_sms"] = args.comm_sms
+    dp = DataParallelIPC(cfg, device=dev, **dp_kw)
     w_init = [w.to(dev, dtype) for w in S.fan_in_normal(dims, seed=1)]
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     pool = []
@@ -488,9 +491,10 @@ def run_c5(args, world, rank, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "configs[4] wide batch-sharded: dims (1000,4096x6,4096), global batch 65536, T=4, "
-                               "tanh, bf16 storage / fp32 accumulation, per-layer fp32 dW all-reduce (NCCL)",
+                               "tanh, bf16 storage / fp32 accumulation, per-layer fp32 dW reduction (NCCL)",
                    "global_batch": Bg, "batch_per_rank": B, "T": T, "parallelism": f"dp{world}",
                    "comm_sms": dp.comm_sms if world > 1 else 0,
+                   "dp_reduce": dp.reduce if world > 1 else None,
                    "l2": "inputs larger than L2 (the per-step state is GBs)"},
         "roofline": roof,
         "e2e": {"value": round(n_e2e * Bg / (ms_e2e * 1e-3), 1), "unit": "samples/s",
@@ -1047,6 +1051,8 @@ def main():
     ap.add_argument("--chunk", type=int, default=500, help="training steps per persistent-kernel launch")
     ap.add_argument("--comm-sms", type=int, default=-1,
                     help="c5: SMs the delta GEMMs leave to the overlapped all-reduces (default: DataParallelIPC's)")
+    ap.add_argument("--dp-reduce", choices=["rs_ag", "allreduce"], default="rs_ag",
+                    help="c5: reduce-scatter + sliced apply + all-gather, or one all-reduce per layer")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

@@ -9,14 +9,22 @@ all batch columns:
 
 Each rank forms its fp32 partial ``dW_r[l]`` (``ipc_weight_delta`` /
 ``IPC_MODE_WDELTA``, tensor cores for wide layers), the partials are summed
-with one all-reduce per layer (issued as soon as that layer's partial is
+with one reduction per layer (issued as soon as that layer's partial is
 ready, so the reductions of earlier layers overlap the GEMMs of later ones),
 and every rank applies the same sum (``ipc_weight_apply``), keeping the
 replicas identical.  While reductions are in flight the persistent GEMMs
 leave ``comm_sms`` SMs free (``ipc_set_max_ctas``): with every SM taken by a
 GEMM CTA, the collective's kernels would wait for the GEMM and the overlap
 would be lost.  Each layer's sum is applied as soon as its own reduction is
-done.  The reference is single-GPU; this is the scaling path of
+done.
+
+``reduce="rs_ag"`` (the default when a layer's size divides by the world)
+splits the all-reduce into its halves around the apply: a reduce-scatter of
+the fp32 deltas gives each rank the summed delta of 1/world of the weights,
+the rank applies it to that slice only, and an all-gather of the updated
+16-bit slices rebuilds the replicas.  NVLink carries 4 + 2 bytes per weight
+element instead of 4 + 4, the apply touches 1/world of W, and every element
+of W is computed once, so the replicas stay identical by construction.  The reference is single-GPU; this is the scaling path of
 the wide configuration (batch 65536 over 1/2/4/8 B200s).
 """
 from __future__ import annotations
@@ -43,15 +51,19 @@ def allreduce_deltas(deltas: list[torch.Tensor], group=None, *, async_op: bool =
 
 
 class DataParallelIPC:
-    """Replicated weights, batch shards, one fp32 dW all-reduce per layer per training step."""
+    """Replicated weights, batch shards, one fp32 dW reduction per layer per training step."""
 
     def __init__(self, cfg: IPCConfig, *, device: torch.device, group=None, seed: int = 0,
-                 model: TileLangIPC | None = None, comm_sms: int = 24):
-        """comm_sms: SMs the delta GEMMs leave to the all-reduces they overlap (world > 1)."""
+                 model: TileLangIPC | None = None, comm_sms: int = 24, reduce: str = "rs_ag"):
+        """comm_sms: SMs the delta GEMMs leave to the reductions they overlap (world > 1).
+        reduce: "rs_ag" (reduce-scatter, sliced apply, all-gather) or "allreduce"."""
         if comm_sms < 0:
             raise ValueError("comm_sms must be >= 0")
+        if reduce not in ("rs_ag", "allreduce"):
+            raise ValueError(f"unknown reduce {reduce!r}")
         self.group = group
         self.comm_sms = int(comm_sms)
+        self.reduce = reduce
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
         self.model = model if model is not None else TileLangIPC(cfg, device=device, seed=seed)
@@ -98,6 +110,26 @@ class DataParallelIPC:
         N.check(N.load().ipc_weight_apply(w.data_ptr(), dw.data_ptr(), w.numel(), N.dtype_code(w.dtype),
                                           N.stream_handle(w.device)))
 
+    def _apply_slice(self, l: int, lo: int, hi: int) -> None:
+        """W[l].flat[lo:hi] = cast(W[l].flat[lo:hi] + dW[l].flat[lo:hi])."""
+        w, dw = self.model.w[l].view(-1), self._dw[l].view(-1)
+        N.check(N.load().ipc_weight_apply(w[lo:hi].data_ptr(), dw[lo:hi].data_ptr(), hi - lo,
+                                          N.dtype_code(w.dtype), N.stream_handle(w.device)))
+
+    # -- the two collectives of the sliced update (overridable for backends without them) --
+    def _reduce_scatter(self, l: int, lo: int, hi: int):
+        """dW[l].flat[lo:hi] = sum over ranks of dW[l].flat[lo:hi] (this rank's slice), async."""
+        flat = self._dw[l].view(-1)
+        return dist.reduce_scatter_tensor(flat[lo:hi], flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+
+    def _all_gather(self, l: int, lo: int, hi: int):
+        """Every rank's updated slice of W[l] into every replica, async."""
+        flat = self.model.w[l].view(-1)
+        return dist.all_gather_into_tensor(flat, flat[lo:hi], group=self.group, async_op=True)
+
+    def _sliced(self, l: int) -> bool:
+        return self.world > 1 and self.reduce == "rs_ag" and self._dw[l].numel() % self.world == 0
+
     @torch.no_grad()
     def train_step(self, x_local: torch.Tensor, y_local: torch.Tensor, *, T: int = 4) -> None:
         """Forward sweep + T inference iterations on the local shard, then the all-reduced weight update
@@ -115,19 +147,32 @@ class DataParallelIPC:
         try:
             for l in order:
                 self._delta(l, self._dw[l])
-                hs = allreduce_deltas([self._dw[l]], self.group, async_op=True)
-                if hs:
-                    handles[l] = hs[0]
-                    if not capped and self.comm_sms > 0:
-                        self._cap(self.comm_sms)
-                        capped = True
+                if self._sliced(l):
+                    n = self._dw[l].numel() // self.world
+                    handles[l] = self._reduce_scatter(l, self.rank * n, (self.rank + 1) * n)
+                else:
+                    hs = allreduce_deltas([self._dw[l]], self.group, async_op=True)
+                    if hs:
+                        handles[l] = hs[0]
+                if l in handles and not capped and self.comm_sms > 0:
+                    self._cap(self.comm_sms)
+                    capped = True
         finally:
             if capped:
                 self._cap(0)
+        gathers = []
         for l in order:
             if l in handles:
                 handles[l].wait()
-            self._apply(l, self._dw[l])
+            if self._sliced(l):
+                n = self._dw[l].numel() // self.world
+                lo, hi = self.rank * n, (self.rank + 1) * n
+                self._apply_slice(l, lo, hi)
+                gathers.append(self._all_gather(l, lo, hi))
+            else:
+                self._apply(l, self._dw[l])
+        for h in gathers:
+            h.wait()
         m.steps_done += 1
 
     def state_dict(self) -> dict:

@@ -1,10 +1,12 @@
 """Host-side logic of the batch-sharded data-parallel step on 2 CPU ranks (gloo).
 
-The GPU kernels are replaced by the CPU oracle behind the same two hooks the
-product uses (``_delta`` for a rank's dW, ``_apply`` for W += dW), so the test
-checks the orchestration that runs on the GPUs: local forward sweep and T
-iterations, one all-reduce per layer, identical apply on every rank -- and
-that the sharded step equals the oracle's full-batch step.
+The GPU kernels are replaced by the CPU oracle behind the same hooks the
+product uses (``_delta`` for a rank's dW, ``_apply`` / ``_apply_slice`` for
+W += dW), so the test checks the orchestration that runs on the GPUs: local
+forward sweep and T iterations, then per layer either one all-reduce and an
+identical apply on every rank, or a reduce-scatter, the apply of this rank's
+slice and an all-gather of the updated weights -- and that the sharded step
+equals the oracle's full-batch step in both forms.
 """
 import os
 import socket
@@ -49,7 +51,7 @@ class _OracleModel:
         self.x, _, self.e, _ = O.ipc_step(self.x, self.w, act=ACT, alpha=ALPHA, gamma=GAMMA, update_weights=False)
 
 
-def _worker(rank, world, port, data, out):
+def _worker(rank, world, port, data, out, reduce):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -65,6 +67,10 @@ def _worker(rank, world, port, data, out):
                 self.model.w[l] += dw
                 caps.append(("apply", l))
 
+            def _apply_slice(self, l, lo, hi):
+                self.model.w[l].view(-1)[lo:hi] += self._dw[l].view(-1)[lo:hi]
+                caps.append(("apply", l))
+
             def _cap(self, leave):
                 caps.append(("cap", leave))
 
@@ -73,7 +79,7 @@ def _worker(rank, world, port, data, out):
         w0, x, y = data
         cols = slice(rank * B // world, (rank + 1) * B // world)
         model = _OracleModel(w0 if rank == 0 else [torch.zeros_like(t) for t in w0])  # rank 0 broadcasts
-        dp = _DP(_Cfg(), device=torch.device("cpu"), model=model)
+        dp = _DP(_Cfg(), device=torch.device("cpu"), model=model, reduce=reduce)
         dp.train_step(x[:, cols].contiguous(), y[:, cols].contiguous(), T=T)
         out[rank] = ([t.clone() for t in dp.model.w], [t.clone() for t in dp.model.x], caps)
     finally:
@@ -87,7 +93,8 @@ def _free_port():
 
 
 @pytest.mark.timeout(120)
-def test_sharded_step_equals_full_batch_step():
+@pytest.mark.parametrize("reduce", ["rs_ag", "allreduce"])
+def test_sharded_step_equals_full_batch_step(reduce):
     torch.manual_seed(0)
     w0 = [torch.randn(a, b) / b ** 0.5 for a, b in zip(DIMS[:-1], DIMS[1:])]
     x = torch.rand(DIMS[-1], B)
@@ -95,7 +102,7 @@ def test_sharded_step_equals_full_batch_step():
     ctx = mp.get_context("spawn")
     with ctx.Manager() as mgr:
         out = mgr.dict()
-        mp.start_processes(_worker, args=(2, _free_port(), (w0, x, y), out), nprocs=2, join=True,
+        mp.start_processes(_worker, args=(2, _free_port(), (w0, x, y), out, reduce), nprocs=2, join=True,
                            start_method="spawn")
         res = dict(out)
     x_ref, w_ref, _, _ = O.train_step(x, y, w0, act=ACT, alpha=ALPHA, gamma=GAMMA, T=T)

@@ -3,7 +3,8 @@
 One GPU: DataParallelIPC with a single rank is exactly TileLangIPC.train_step.
 Two GPUs (skipped with fewer): two NCCL ranks, each with half of the batch,
 end with the same weights as the full batch on one GPU (1e-2, 16-bit gate)
-and bit-identical replicas.
+and bit-identical replicas, with the all-reduce update and with the
+reduce-scatter / sliced apply / all-gather update.
 """
 import os
 import socket
@@ -54,7 +55,7 @@ def test_single_rank_equals_trainer_step():
         assert O.rel_inf(a.float().cpu(), b) <= 1e-2
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, reduce):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
 
@@ -66,7 +67,7 @@ def _worker(rank, world, port, out):
     try:
         from lich_b200.data_parallel import DataParallelIPC
         w0, x, y = _data()
-        dp = DataParallelIPC(_cfg(), device=dev)
+        dp = DataParallelIPC(_cfg(), device=dev, reduce=reduce)
         for dst, src in zip(dp.model.w, w0):
             dst.copy_(src.to(dev, torch.bfloat16))
         cols = slice(rank * B // world, (rank + 1) * B // world)
@@ -80,13 +81,14 @@ def _worker(rank, world, port, out):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.timeout(300)
-def test_two_ranks_match_full_batch():
+@pytest.mark.parametrize("reduce", ["rs_ag", "allreduce"])
+def test_two_ranks_match_full_batch(reduce):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     with mp.get_context("spawn").Manager() as mgr:
         out = mgr.dict()
-        mp.start_processes(_worker, args=(2, port, out), nprocs=2, join=True, start_method="spawn")
+        mp.start_processes(_worker, args=(2, port, out, reduce), nprocs=2, join=True, start_method="spawn")
         res = dict(out)
     ref = _full_batch_reference(torch.device("cuda", 0))
     for a, b in zip(res[0], res[1]):
