@@ -195,5 +195,5 @@ def test_cta_cap_keeps_results():
                 assert O.rel_inf(got["out"], ref) <= (1e-3 if mode == N.MODE_WDELTA else 1e-2), (cap, mode)
     finally:
         N.set_max_ctas(0)
-    with pytest.raises(N.IpcError):
+    with pytest.raises(ValueError):  # IPC_ERR_ARG
         N.set_max_ctas(-1)
