@@ -861,10 +861,10 @@ def _c3_algo(kind, M, K, B):
     weight = kind.startswith("W")
     mg, ng, kg = (M, K, B) if weight else (M, B, K)
     if weight and kg >= 1024 and mg >= 16 and ng >= 16:
-        return "tcgen05 split-K" if -(-mg // 128) * -(-ng // 128) < 74 else "tcgen05"
+        return "tcgen05 split-K" if -(-mg // 128) * -(-ng // 256) < 74 else "tcgen05"
     if weight and B <= 16:
         return "outer"
-    if mg >= 128 and ng >= 128 and kg >= 64 and mg * ng * kg >= 128 * 256 * 256:
+    if mg >= 64 and ng >= 128 and kg >= 64 and mg * ng * kg >= 128 * 256 * 256:
         return "tcgen05"
     return "mma.sync"
 

@@ -849,8 +849,9 @@ bool tc_eligible(int mode, int M, int K, int B, int dtype, int algo, bool b_acti
   if (algo == IPC_ALGO_AUTO) {
     // a weight update with a long batch reduction spreads it over the SMs (split-K)
     if (weight && splitk && Kg >= 1024 && Mg >= 16 && Ng >= 16) return true;
-    // below ~128 x 256 x 256 the generic kernel's lower latency wins
-    if (Mg < 128 || Ng < 128 || Kg < 64) return false;
+    // below ~128 x 256 x 256 the generic kernel's lower latency wins; 64 <= M < 128 still pays on
+    // tensor cores (the tile's missing rows are TMA zero fill, masked in the epilogue)
+    if (Mg < 64 || Ng < 128 || Kg < 64) return false;
     if ((double)Mg * Ng * Kg < 128.0 * 256 * 256) return false;
   }
   return true;

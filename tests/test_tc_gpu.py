@@ -16,7 +16,8 @@ from oracle import ipc_oracle as O
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 DTYPES = [torch.float16, torch.bfloat16]
-SHAPES = [(128, 64, 128), (256, 512, 512), (1000, 1000, 264), (384, 200, 136), (128, 4096, 256)]
+SHAPES = [(128, 64, 128), (256, 512, 512), (1000, 1000, 264), (384, 200, 136), (128, 4096, 256), (64, 256, 264),
+          (72, 128, 136)]
 
 
 def _N():
