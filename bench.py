@@ -1,26 +1,30 @@
 """Benchmark of the iPC training step on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2] [--depth 6] [--act tanh]
+                    [--config c5|c2|c3|c4a|c4b] [--depth 6] [--act tanh]
 
 A *step* is one training step on one batch: T = 4 inference iterations
 (prediction + state update over all layers) followed by one weight update,
 after the forward-init sweep of the batch (the oracle schedule
 ``for t in range(T): ipc_step(update_weights=(t == T-1))``).
 
-Default workload = ``configs[1]`` of the baseline: dims (10, 64 x depth, 784),
-depth 6, B = 128, fp16 storage / fp32 accumulation, alpha 1e-4, gamma 0.5,
-T = 4, f = tanh, 10 000 steps.  Inputs are seeded synthetic batches (MNIST is
-not available offline): a device pool of 1024 batches (205 MB, larger than
-the 126 MB L2), so every step reads a fresh batch from HBM.
+Default workload = ``configs[4]`` of the baseline at every N: dims
+(1000, 4096 x 6, 4096), global batch 65536 split over the N ranks (one process
+per GPU under torchrun), bf16 storage / fp32 accumulation, tanh, alpha 1e-4,
+gamma 0.5, T = 4, with one fp32 weight-delta reduction per layer per step over
+NCCL (``DataParallelIPC``).  It fits one GPU and is the largest single-GPU
+configuration; its per-step state (GBs) is far larger than the 126 MB L2.
+At N = 1 the line also carries ``secondary``: configs[1] (hidden 64, depth 6,
+B = 128, fp16) measured in the same run, with its own e2e and CPU baseline.
 
-``value``: samples/s with the pool resident in HBM (persistent kernel,
-``TileLangIPC.train_pool``).  ``e2e``: the same through the public API with
-pinned host batches copied to the device and each step's energy copied back
-inside the timed region.  ``--gpus N`` runs N independent replicas (the
-hidden-64 network does not shard; weak scaling).  ``--impl reference`` times
-the reference's algorithm (the CPU oracle, a PyTorch restatement of
-``reference.py``) on the host cores.
+``--config c2`` is the configs[1] line alone (``--gpus N`` runs N independent
+replicas there: the hidden-64 network does not shard); c3 the per-kernel
+microbench, c4a / c4b configs[3].  Inputs are seeded synthetic batches (MNIST
+is not available offline).  ``value``: samples/s with the batches resident in
+HBM; ``e2e``: the same through the public API with pinned host batches copied
+to the device and a result copied back inside the timed region.
+``--impl reference`` times the reference's algorithm (the CPU oracle, a
+PyTorch restatement of ``reference.py``) on the host cores.
 """
 from __future__ import annotations
 
@@ -60,18 +64,59 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clock and throttle reasons sampled while the timed region runs.
+
+    NVML is polled from a thread every 20 ms (a timed region of a fraction of a second still gets
+    samples); without NVML, ``nvidia-smi -lms 200`` in a subprocess.  Every sample falls inside the
+    timed region (the sampler starts right before it and stops right after it)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, period_s: float = 0.02):
         self.index = index
+        self.period = period_s
+        self.rows: list[tuple[float, float, int]] = []  # (sm MHz, max MHz, reason bits)
         self.proc = None
         self.path = None
+        self._thread = None
+        self._stop = None
+        self._nvml = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:  # NVML numbers GPUs physically; match torch's device by UUID when it exposes one
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _poll(self, nv, h):
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((float(sm), float(mx), int(bits)))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
 
     def __enter__(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            self._nvml = nv
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
+            self._thread.start()
+            return self
+        except Exception:
+            self._nvml = None
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
@@ -84,32 +129,35 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            for line in Path(self.path).read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    bits = sum(bit for (_, bit), v in zip(self.REASONS, parts[5:9]) if v.lower() == "active")
+                    self.rows.append((float(parts[1]), float(parts[2]), bits))
+                except ValueError:
+                    continue
+            os.unlink(self.path)
 
     def summary(self):
-        if self.proc is None or self.path is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        for line in Path(self.path).read_text().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
-            except ValueError:
-                continue
-        os.unlink(self.path)
-        if not rows:
+        if self._thread is None and self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source (NVML / nvidia-smi)"]}
+        if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "samples": len(rows), "reasons": reasons}
+        reasons = sorted({n for _, _, bits in self.rows for n, b in self.REASONS if bits & b})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": max(r[1] for r in self.rows),
+                "samples": len(self.rows), "source": "nvml" if self._thread is not None else "nvidia-smi",
+                "reasons": reasons}
 
 
 def dist_setup(args):
@@ -169,16 +217,17 @@ def step_costs(dims, B, T, elem):
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_baseline(dims, B, T, act, budget_s=12.0, max_steps=None):
+def cpu_baseline(dims, B, T, act, budget_s=12.0, max_steps=None, search_threads=True):
     """The reference algorithm (oracle restatement of reference.py, fp32) on all host cores."""
     from lich_b200 import synthetic as S
     from oracle import ipc_oracle as O
     model, ncpu = cpu_info()
     w = S.fan_in_normal(dims, seed=1)
     pool = S.batch_pool(dims[-1], dims[0], B, count=4, seed=2)
-    # small GEMMs can run slower on many threads: keep the fastest of a few thread counts
+    # small GEMMs can run slower on many threads: keep the fastest of a few thread counts (large
+    # GEMMs use every core: no search)
     best = (0.0, ncpu)
-    for th in sorted({ncpu, min(ncpu, 16), min(ncpu, 8), min(ncpu, 4)}, reverse=True):
+    for th in (sorted({ncpu, min(ncpu, 16), min(ncpu, 8), min(ncpu, 4)}, reverse=True) if search_threads else ()):
         torch.set_num_threads(th)
         O.train_step(pool[0][0], pool[0][1], w, act=act, alpha=1e-4, gamma=0.5, T=T)
         t0, k = time.perf_counter(), 0
@@ -191,6 +240,8 @@ def cpu_baseline(dims, B, T, act, budget_s=12.0, max_steps=None):
     cores = best[1]
     torch.set_num_threads(cores)
     w = S.fan_in_normal(dims, seed=1)
+    if not search_threads:  # one untimed step (allocator and thread-pool warm-up)
+        O.train_step(pool[0][0], pool[0][1], w, act=act, alpha=1e-4, gamma=0.5, T=T)
     t0 = time.perf_counter()
     n = 0
     w_init = [t.clone() for t in w]
@@ -287,6 +338,7 @@ def run_c2(args, world, rank, local):
             "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
             "frac": round((achieved_gbs / pk["hbm_gbs"]) if bound == "hbm" else (achieved_tfs / pk["bf16_tflops"]), 4),
             "traffic": TRAFFIC_PER_STEP.get(("c2", args.depth)) and round(TRAFFIC_PER_STEP[("c2", args.depth)] * units),
+            "traffic_source": "constant from an earlier ncu capture of this kernel, scaled to the launch",
             "peak_source": pk["source"], "kernel": "net_kernel (ipc_net_train)",
             "algorithmic_bytes_per_step": bytes_step, "algorithmic_flop_per_step": flop_step,
             "steps_per_launch": units, "avg_launch_ms": round(avg_ms, 4),
@@ -312,75 +364,59 @@ def run_c2(args, world, rank, local):
 
 
 # ncu dram__bytes_read.sum + dram__bytes_write.sum per training step of the persistent
-# kernel, from the captures summarised in profiles/ (filled in after each capture).
+# kernel: constants from an earlier ncu capture of the same kernel (not measured in this run; a run
+# cannot read DRAM counters without a profiler).
 TRAFFIC_PER_STEP: dict = {
-    # profiles/net_kernel_c2_depth6.md: 10,404,864 B read + 0 B written over a 50-step launch
+    # depth 6: 10,404,864 B read + 0 B written over a 50-step launch
     ("c2", 6): 10404864 / 50,
 }
 
 
 def run_c2_e2e(args, model, dims, B, T, dtype, dev, rank, world):
-    """Public API, host batches: pinned host pool -> device ring (H2D in the timed region),
-    train_pool over the chunk, per-step energy copied back (D2H in the timed region)."""
+    """Public API, host batches: ``BatchPipeline`` copies pinned host batches into a double-buffered device
+    ring on its copy stream (H2D in the timed region), ``train_pool`` trains on each slot of 64 batches in
+    one launch, and each step's energy is copied back (D2H in the timed region)."""
     from lich_b200 import synthetic as S
+    from lich_b200.input_pipeline import BatchPipeline
     Ph = 64
     x_h, y_h = S.stacked_pool(dims[-1], dims[0], B, count=Ph, nets=1, seed=77 + rank, dtype=dtype)
     x_h = x_h[:, 0].contiguous().pin_memory()
     y_h = y_h[:, 0].contiguous().pin_memory()
     chunk = 64
     steps = max(chunk, (min(args.steps, 4096) // chunk) * chunk)
-    ring_x = [torch.empty((chunk, dims[-1], B), device=dev, dtype=dtype) for _ in range(2)]
-    ring_y = [torch.empty((chunk, dims[0], B), device=dev, dtype=dtype) for _ in range(2)]
     energy = [torch.empty((chunk,), device=dev, dtype=torch.float32) for _ in range(2)]
     energy_h = torch.empty((steps,), dtype=torch.float32).pin_memory()
     comp = torch.cuda.current_stream(dev)
-    copy = torch.cuda.Stream(dev)
-    ready = [torch.cuda.Event() for _ in range(2)]
-    free = [torch.cuda.Event() for _ in range(2)]
-
-    def h2d(slot, c):
-        with torch.cuda.stream(copy):
-            copy.wait_event(free[slot])
-            for j in range(chunk):
-                b = (c * chunk + j) % Ph
-                ring_x[slot][j].copy_(x_h[b], non_blocking=True)
-                ring_y[slot][j].copy_(y_h[b], non_blocking=True)
-            ready[slot].record(copy)
-
-    for s in range(2):
-        free[s].record(comp)
+    w_init = [w.clone() for w in model.w]
+    source = ((x_h, y_h) for _ in range(steps // chunk))  # pool chunks of 64 pinned batches (Ph == chunk)
     torch.cuda.synchronize(dev)
     barrier(world)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record(comp)
-    nchunks = steps // chunk
-    w_init = [w.clone() for w in model.w]
-    h2d(0, 0)
-    for c in range(nchunks):
-        slot = c % 2
+    pipe = BatchPipeline(source, device=dev, dtype=dtype, num_classes=dims[0], depth=2, steps_per_slot=chunk)
+    for c, (px, py) in enumerate(pipe):
         if c % max(1, RESET_EVERY // chunk) == 0:
             for w, w0 in zip(model.w, w_init):
                 w.copy_(w0)
-        if c + 1 < nchunks:
-            h2d((c + 1) % 2, c + 1)
-        comp.wait_event(ready[slot])
-        model.train_pool(ring_x[slot], ring_y[slot], steps=chunk, T=T, energy=energy[slot])
-        energy_h[c * chunk:(c + 1) * chunk].copy_(energy[slot], non_blocking=True)
-        free[slot].record(comp)
+        model.train_pool(px, py, steps=int(px.shape[0]), T=T, energy=energy[c % 2])
+        energy_h[c * chunk:c * chunk + int(px.shape[0])].copy_(energy[c % 2][:int(px.shape[0])], non_blocking=True)
     end.record(comp)
     torch.cuda.synchronize(dev)
     ms = max_over_ranks(start.elapsed_time(end), world, dev)
     assert torch.isfinite(energy_h).all()
     h2d_b = (dims[-1] + dims[0]) * B * 2
+    assert pipe.h2d_bytes == h2d_b * steps
     return {"value": round(world * steps * B / (ms * 1e-3), 1), "unit": "samples/s", "h2d_bytes_per_step": h2d_b,
             "d2h_bytes_per_step": 4, "steps": steps,
-            "path": "TileLangIPC.train_pool over pinned-host batches copied per chunk of 64 steps "
-                    "(copy stream, double-buffered), per-step energy read back"}
+            "path": "lich_b200.input_pipeline.BatchPipeline (pinned host pools of 64 batches, one copy per tensor on "
+                    "a copy stream, two device slots) feeding TileLangIPC.train_pool, per-step energy read back"}
 
 
 C5_DIMS = (1000,) + (4096,) * 6 + (4096,)
 C5_BATCH = 65536
+C5_WORKLOAD = ("configs[4] wide batch-sharded: dims (1000,4096x6,4096), global batch 65536, T=4, tanh, "
+               "bf16 storage / fp32 accumulation, per-layer fp32 dW reduction (NCCL)")
 
 
 def run_c5(args, world, rank, local):
@@ -441,6 +477,11 @@ def run_c5(args, world, rank, local):
     launches = N.launch_count() - launches0
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
     assert N.device_status() == 0
+    # one more (untimed) step with phase marks: where the per-rank step time goes
+    marks: list = []
+    restore()
+    dp.train_step(*pool[0], T=T, phases=marks)
+    breakdown = {k: round(max_over_ranks(v, world, dev), 3) for k, v in dp.phase_times(marks).items()}
     flop_rank, bytes_rank = step_costs(dims, B, T, 2)
     pk = peaks()
     tfs = flop_rank / (ms / args.steps * 1e-3) / 1e12
@@ -490,11 +531,11 @@ def run_c5(args, world, rank, local):
         "metric": METRIC, "value": round(args.steps * Bg / (ms * 1e-3), 1), "unit": "samples/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "configs[4] wide batch-sharded: dims (1000,4096x6,4096), global batch 65536, T=4, "
-                               "tanh, bf16 storage / fp32 accumulation, per-layer fp32 dW reduction (NCCL)",
+        "config": {"workload": C5_WORKLOAD,
                    "global_batch": Bg, "batch_per_rank": B, "T": T, "parallelism": f"dp{world}",
                    "comm_sms": dp.comm_sms if world > 1 else 0,
                    "dp_reduce": dp.reduce if world > 1 else None,
+                   "step_breakdown_ms": breakdown,
                    "l2": "inputs larger than L2 (the per-step state is GBs)"},
         "roofline": roof,
         "e2e": {"value": round(n_e2e * Bg / (ms_e2e * 1e-3), 1), "unit": "samples/s",
@@ -505,7 +546,7 @@ def run_c5(args, world, rank, local):
         "gpu_launches": int(launches), "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(dims, 512, T, "tanh", budget_s=12.0)
+        line["cpu_baseline"] = cpu_baseline(dims, 512, T, "tanh", budget_s=12.0, search_threads=False)
         line["cpu_baseline"]["sample"] += " (B=512 sample of the 65536-column batch; per-sample cost)"
     return line
 
@@ -613,9 +654,11 @@ def run_c4b(args, world, rank, local):
             "unit": "GB/s" if hbm_bound else "TFLOP/s",
             "frac": round(gbs / pk["hbm_gbs"], 4) if hbm_bound else round(tfs / pk["bf16_tflops"], 4),
             "tensor_frac": round(tfs / pk["bf16_tflops"], 4),
-            # profiles/net_kernel_c4b_296nets.md: per network and launch, 203,264 B of batch per step plus
-            # 118,690 B (weights read) + 279,658 B (written back) once, scaled to this launch
+            # a constant, not measured in this run: the ncu DRAM bytes (read + write) of one network of an
+            # earlier capture of this kernel -- 203,264 B of batch per step plus 118,690 B (weights read)
+            # and 279,658 B (written back) once per launch -- scaled to this launch
             "traffic": round(nets * (full[0][1] * 203264 + 118690 + 279658)),
+            "traffic_source": "constant from an earlier ncu capture of this kernel, scaled to the launch",
             "peak_source": pk["source"], "kernel": "net_kernel (ipc_net_train, nets per launch = %d)" % nets,
             "algorithmic_flop_per_network_step": flop_net, "network_steps_per_launch": units,
             "avg_launch_ms": round(avg_ms, 4),
@@ -970,12 +1013,16 @@ def run_reference(args, world, rank):
         return None
     from lich_b200 import synthetic as S
     if args.config == "c5":
-        cb = cpu_baseline(C5_DIMS, 512, 4, "tanh", budget_s=max(10.0, min(120.0, 5.0 * args.steps)))
+        cb = cpu_baseline(C5_DIMS, 512, 4, "tanh", budget_s=max(10.0, min(60.0, 10.0 + 1.0 * args.steps)),
+                          search_threads=False)
+        cb["sample"] += " (B=512 sample of the 65536-column batch; per-sample cost)"
+        Bg = args.batch or C5_BATCH
         return {"metric": METRIC, "value": round(cb["value"], 1), "unit": "samples/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(512 / cb["value"] * 1e3, 4),
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(Bg / cb["value"] * 1e3, 4),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic", "impl": "reference",
-                "config": {"workload": "configs[4] wide: dims (1000,4096x6,4096), T=4, tanh (B=512 sample)"},
+                "config": {"workload": C5_WORKLOAD, "global_batch": Bg, "T": 4,
+                           "parallelism": "host CPU (rank 0), all cores"},
                 "cpu_baseline": cb,
                 "e2e": {"value": round(cb["value"], 1), "unit": "samples/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
@@ -1022,6 +1069,19 @@ def run_reference(args, world, rank):
                     "d2h_bytes_per_step": 0}}
 
 
+def secondary_c2(args, world, rank, local):
+    """configs[1] (hidden 64, depth 6, B = 128, fp16) in the same run as the default line: 2000 training
+    steps in launches of 500 (the steady state of the persistent kernel), its e2e and CPU baseline."""
+    import copy
+    a = copy.copy(args)
+    a.config, a.steps, a.chunk, a.depth, a.act = "c2", 2000, 500, 6, "tanh"
+    torch.cuda.empty_cache()
+    c2 = run_c2(a, world, rank, local)
+    keep = ("metric", "value", "unit", "steps", "ms_per_step", "dtype", "config", "roofline", "e2e", "gpu_launches",
+            "clocks", "cpu_baseline")
+    return {k: c2[k] for k in keep if k in c2}
+
+
 def _emit(fd: int, line: dict) -> None:
     """The result line, alone, on the original standard output."""
     os.write(fd, (json.dumps(line) + "\n").encode())
@@ -1038,10 +1098,12 @@ def main():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c3", "c4a", "c4b", "c5"], default="c2",
-                    help="c2: configs[1] hidden-64 (default); c3: configs[2] per-kernel microbench; "
-                         "c4a: configs[3] small batch; c4b: configs[3] 4096 networks; "
-                         "c5: configs[4] wide data-parallel")
+    ap.add_argument("--config", choices=["c2", "c3", "c4a", "c4b", "c5"], default="c5",
+                    help="c5: configs[4] wide batch-sharded data parallel (default); c2: configs[1] hidden-64; "
+                         "c3: configs[2] per-kernel microbench; c4a: configs[3] small batch; "
+                         "c4b: configs[3] 4096 networks")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="c5 at N=1: skip the configs[1] measurement carried as `secondary`")
     ap.add_argument("--nets", type=int, default=0, help="c4b: number of networks (default 4096)")
     ap.add_argument("--sizes", default="", help="c3: comma-separated M=K list")
     ap.add_argument("--batches", default="", help="c3 / c4a: comma-separated B list")
@@ -1064,12 +1126,14 @@ def main():
             _emit(result_fd, line)
         return
     if "--steps" not in sys.argv:
-        args.steps = {"c5": 5, "c4b": 200, "c4a": 500}.get(args.config, args.steps)
+        args.steps = {"c5": 20, "c4b": 200, "c4a": 500}.get(args.config, args.steps)
     if args.config == "c4b" and "--chunk" not in sys.argv:
         args.chunk = 50
     world, rank, local = dist_setup(args)
     runners = {"c2": run_c2, "c3": run_c3, "c4a": run_c4a, "c4b": run_c4b, "c5": run_c5}
     line = runners[args.config](args, world, rank, local)
+    if args.config == "c5" and world == 1 and not args.no_secondary:
+        line["secondary"] = secondary_c2(args, world, rank, local)
     if rank == 0:
         _emit(result_fd, line)
     if world > 1:

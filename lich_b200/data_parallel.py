@@ -131,15 +131,29 @@ class DataParallelIPC:
         return self.world > 1 and self.reduce == "rs_ag" and self._dw[l].numel() % self.world == 0
 
     @torch.no_grad()
-    def train_step(self, x_local: torch.Tensor, y_local: torch.Tensor, *, T: int = 4) -> None:
+    def train_step(self, x_local: torch.Tensor, y_local: torch.Tensor, *, T: int = 4,
+                   phases: list | None = None) -> None:
         """Forward sweep + T inference iterations on the local shard, then the all-reduced weight update
-        with the last iteration's errors and states (the oracle schedule, full batch = all shards)."""
+        with the last iteration's errors and states (the oracle schedule, full batch = all shards).
+
+        ``phases``: if a list is given, CUDA events (on the current stream) are appended as
+        ``(name, event)`` at the start, after the inference iterations, after the last delta GEMM was
+        issued and at the end; ``phase_times`` turns them into milliseconds."""
         if T < 1:
             raise ValueError("T must be >= 1")
         m = self.model
+
+        def mark(name):
+            if phases is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                phases.append((name, ev))
+
+        mark("start")
         m.initialize_batch(x_local, y_local)
         for _ in range(T):
             m.step_initialized(update_weights=False)
+        mark("inference")
         L = len(self.cfg.dims) - 1
         order = sorted(range(L), key=lambda l: -self._dw[l].numel())  # biggest reductions start first
         handles = {}
@@ -160,6 +174,7 @@ class DataParallelIPC:
         finally:
             if capped:
                 self._cap(0)
+        mark("deltas")
         gathers = []
         for l in order:
             if l in handles:
@@ -173,7 +188,14 @@ class DataParallelIPC:
                 self._apply(l, self._dw[l])
         for h in gathers:
             h.wait()
+        mark("end")
         m.steps_done += 1
+
+    @staticmethod
+    def phase_times(phases: list) -> dict:
+        """Milliseconds between consecutive marks of ``train_step(phases=...)`` (synchronises)."""
+        torch.cuda.synchronize()
+        return {f"{a[0]}->{b[0]}": a[1].elapsed_time(b[1]) for a, b in zip(phases, phases[1:])}
 
     def state_dict(self) -> dict:
         return self.model.state_dict()

@@ -154,6 +154,7 @@ class TileLangIPC:
         self._steady_state_runner = None
         self._steady_state_graph_key: tuple | None = None
         self._steady_state_graph_steps: int | None = None
+        self._graph_pool = None  # private memory pool shared by this model's captured graphs
         self._net_desc = None
         self._net_keep = None
         self.steps_done = 0
@@ -562,43 +563,50 @@ class TileLangIPC:
                 self.train_step(pool_x[b], pool_y[b], T=T)
 
     # ---------------------------------------------------------- steady state
+    # One batch stays loaded and the reference step (P, I, W) is applied to it over and over -- the
+    # reference's latency benchmark (trainer.py:686-826).  Here a block of steps is either a captured
+    # graph (IPCGraphRunner) or, on the persistent-kernel path, a single launch.
+
     def steady_state_graph_ready(self, steps: int) -> bool:
-        return (self._steady_state_runner is not None and self._steady_state_graph_steps == int(steps)
-                and self._steady_state_graph_key == self._runtime_plan_key)
+        return (self._steady_state_runner is not None
+                and self._steady_state_graph_key == (self._runtime_plan_key, int(steps)))
 
     def prepare_steady_state(self, x_input: torch.Tensor, y_target: torch.Tensor, *, steps: int = 1,
                              use_graph: bool | None = None) -> bool:
-        """Reference ``trainer.py:693-724``: initialise the batch; capture ``steps`` steps if graphs are on."""
-        steps = max(1, int(steps))
+        """Load the batch; if graphs are wanted, make sure a captured block of ``steps`` steps matches the
+        current plan.  Returns whether ``run_prepared_steady_state`` will replay a graph."""
         self.initialize_batch(x_input, y_target)
-        if use_graph is None:
-            use_graph = bool(self.cfg.steady_state_graph_default)
-        if not use_graph:
-            return False
-        if not self.steady_state_graph_ready(steps):
-            self._steady_state_runner = self.capture_graph(steps)
-            self._steady_state_graph_steps = steps
-            self._steady_state_graph_key = self._runtime_plan_key
-        return True
+        want = bool(self.cfg.steady_state_graph_default) if use_graph is None else bool(use_graph)
+        if want and not self.steady_state_graph_ready(steps):
+            self._steady_state_runner = self.capture_graph(max(1, int(steps)))
+            self._steady_state_graph_key = (self._runtime_plan_key, max(1, int(steps)))
+            self._steady_state_graph_steps = max(1, int(steps))
+        return want
 
     @torch.no_grad()
     def run_prepared_steady_state(self, *, steps: int | None = None, repeats: int = 1,
                                   use_graph: bool | None = None, collect_metrics: bool = False) -> dict[str, float]:
-        if self.x is None or self.e is None or self._runtime_plan_key is None:
+        """``repeats`` blocks of ``steps`` reference steps on the loaded batch, then a device sync.
+
+        With a graph: one replay per block.  Without one, on the persistent-kernel path all
+        ``steps * repeats`` steps run in one launch (the same arithmetic as separate launches); on the
+        operator path the steps are launched one after another."""
+        if self.x is None or self._runtime_plan_key is None:
             raise RuntimeError("Call prepare_steady_state/initialize_batch first")
-        steps = max(1, int(self._steady_state_graph_steps if steps is None else steps))
-        repeats = max(1, int(repeats))
-        if use_graph is None:
-            use_graph = self.steady_state_graph_ready(steps)
-        if use_graph:
-            if not self.steady_state_graph_ready(steps):
+        block = int(steps) if steps is not None else (self._steady_state_graph_steps or 1)
+        block, repeats = max(1, block), max(1, int(repeats))
+        graph = self.steady_state_graph_ready(block) if use_graph is None else bool(use_graph)
+        if graph:
+            if not self.steady_state_graph_ready(block):
                 raise RuntimeError("Requested graph replay without a matching captured graph")
             for _ in range(repeats):
                 self._steady_state_runner.replay()
+        elif self.net_kernel_eligible(int(self.x[-1].shape[1])):
+            self._net_run(steps=block * repeats, T=1, forward_init=False, update_weights=True)
+            self.steps_done += block * repeats
         else:
-            for _ in range(repeats):
-                for _ in range(steps):
-                    self.step_initialized(collect_metrics=False)
+            for _ in range(block * repeats):
+                self.step_initialized()
         torch.cuda.synchronize(self.device)
         return self.metrics() if collect_metrics else {}
 
@@ -611,34 +619,36 @@ class TileLangIPC:
 
     def run_steady_state_batch(self, x_input, y_target, *, steps: int = 1, repeats: int = 1,
                                use_graph: bool | None = None, collect_metrics: bool = False) -> dict[str, float]:
-        self.prepare_steady_state(x_input, y_target, steps=steps, use_graph=use_graph)
-        return self.run_prepared_steady_state(steps=steps, repeats=repeats, use_graph=use_graph,
+        graph = self.prepare_steady_state(x_input, y_target, steps=steps, use_graph=use_graph)
+        return self.run_prepared_steady_state(steps=steps, repeats=repeats, use_graph=graph,
                                               collect_metrics=collect_metrics)
 
     def precompile(self) -> None:
-        """Run one step with the state saved and restored, so every kernel's one-time
-        attribute setup happens outside any graph capture (reference ``trainer.py:783-818``)."""
-        if self.x is None or self.e is None:
+        """Apply one step to a snapshot of the live tensors and put them back, so every kernel's
+        first-launch setup (function attributes, tensor maps, workspaces) happens now and not inside a
+        later stream capture (reference ``trainer.py:783-818``)."""
+        if self.x is None:
             raise RuntimeError("Call initialize_batch before precompile")
         self._prepare_runtime_plan(int(self.x[-1].shape[1]))
-        live = list(self.w + self.x + self.e) + ([v for v in self.a if v is not None] if self.a is not None else []) \
-            + (list(self._ac) if self._ac is not None else [])
-        saved = [t.clone() for t in live]
-        done = self.steps_done
-        self.step_initialized(collect_metrics=False)
-        torch.cuda.synchronize(self.device)
-        for dst, src in zip(live, saved):
-            dst.copy_(src)
-        self.steps_done = done
+        live = [t for group in (self.w, self.x, self.e, self.a or [], self._ac or []) for t in group if t is not None]
+        snapshot = torch.cat([t.reshape(-1).float() for t in live])
+        steps = self.steps_done
+        self.step_initialized()
+        off = 0
+        for t in live:
+            t.copy_(snapshot[off:off + t.numel()].view(t.shape))
+            off += t.numel()
+        self.steps_done = steps
         torch.cuda.synchronize(self.device)
 
     def capture_graph(self, steps: int):
-        if self.x is None or self.e is None:
-            raise RuntimeError("Call initialize_batch before capture_graph")
+        """A captured block of ``steps`` reference steps on the loaded batch (``IPCGraphRunner``)."""
         from .cuda_graph import IPCGraphRunner
-        runner = IPCGraphRunner(self, steps)
-        runner.capture()
-        return runner
+        if self.x is None:
+            raise RuntimeError("Call initialize_batch before capture_graph")
+        if self._graph_pool is None:
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        return IPCGraphRunner(self, steps, pool=self._graph_pool).capture()
 
     @torch.no_grad()
     def predict(self, x_input: torch.Tensor) -> torch.Tensor:
@@ -671,7 +681,16 @@ class TileLangIPC:
 
 def prepare_batch(images: torch.Tensor, labels: torch.Tensor, *, device: torch.device, dtype: torch.dtype,
                   num_classes: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """NCHW images -> ``[784, B]`` input, labels -> ``[C, B]`` one-hot (reference ``trainer.py:836-846``)."""
-    x = images.flatten(1).T.contiguous().to(device=device, dtype=dtype, non_blocking=True)
+    """A host batch in the trainer's layout (reference ``trainer.py:836-846``): images ``[B, ...]``
+    (NCHW for MNIST) become the input ``[features, B]``, labels ``[B]`` the one-hot target ``[C, B]``.
+
+    The images cross PCIe in their own layout and dtype (one contiguous copy); the transpose to
+    feature-major and the cast to ``dtype`` run on the device.  ``BatchPipeline``
+    (``lich_b200.input_pipeline``) does the same from pinned memory on a copy stream, double-buffered."""
+    if images.ndim < 2 or labels.ndim != 1 or labels.shape[0] != images.shape[0]:
+        raise ValueError("images must be [B, ...] and labels [B]")
+    rows = images.reshape(images.shape[0], -1).to(device, non_blocking=True)
+    x = torch.empty((rows.shape[1], rows.shape[0]), device=device, dtype=dtype)
+    x.copy_(rows.t())
     y = one_hot(labels.to(device, non_blocking=True), num_classes, dtype=dtype)
     return x, y

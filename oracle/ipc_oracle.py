@@ -75,6 +75,20 @@ def one_hot(labels: torch.Tensor, num_classes: int, *, dtype: torch.dtype) -> to
     return torch.nn.functional.one_hot(labels, num_classes=num_classes).to(dtype=dtype).T.contiguous()
 
 
+def init_weights(dims: Sequence[int], *, dtype: torch.dtype, device, seed: int = 0) -> list[torch.Tensor]:
+    """``W[l] ~ kaiming_uniform_(a=sqrt(5))`` = U(-1/sqrt(fan_in), 1/sqrt(fan_in)), drawn in layer order
+    from ONE generator of ``device`` seeded with ``seed``; reference ``reference.py:15-22`` (the trainer
+    consumes the generator in the same order, ``trainer.py:97-108``)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    out = []
+    for n_l, n_u in zip(dims[:-1], dims[1:]):
+        w = torch.empty((n_l, n_u), device=device, dtype=dtype)
+        torch.nn.init.kaiming_uniform_(w, a=5 ** 0.5, generator=g)
+        out.append(w)
+    return out
+
+
 # --------------------------------------------------------------------------
 # Whole-network step (reference.py)
 # --------------------------------------------------------------------------

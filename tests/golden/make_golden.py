@@ -11,8 +11,10 @@ reference (``src/ipc_tilelang/reference.py:42-59``,
 ``src/ipc_tilelang/activations.py:33-35``), drives them with the
 "T inference iterations + 1 weight update" schedule after a forward-init
 sweep (``scripts/validate_reference.py:27-30``), and writes the inputs and
-outputs to ``tests/golden/*.npz``.  The reference is NOT needed to run the
-tests: they only read the committed ``.npz`` files.
+outputs to ``tests/golden/*.npz``.  ``init_weights.npz`` holds the reference's
+own weight init (``init_weights``, ``src/ipc_tilelang/reference.py:15-22``) for
+a few (dims, seed) pairs on the CPU generator.  The reference is NOT needed to
+run the tests: they only read the committed ``.npz`` files.
 """
 from __future__ import annotations
 
@@ -100,8 +102,24 @@ def run_case(name, dims, B, act_name, alpha, gamma, T, steps, batches_n, seed, *
     print(name, {k: v.shape for k, v in arrays.items() if k != "meta"}, meta["energy"])
 
 
+def run_init(name, cases):
+    """The reference's weight init (``init_weights``, ``src/ipc_tilelang/reference.py:15-22``:
+    ``kaiming_uniform_(a=sqrt(5))`` in layer order from one generator) on the CPU, for (dims, seed) pairs."""
+    sys.path.insert(0, str(REF))
+    from ipc_tilelang.reference import init_weights  # noqa: E402
+    arrays, meta = {}, []
+    for c, (dims, seed) in enumerate(cases):
+        for l, w in enumerate(init_weights(dims, dtype=torch.float32, device=torch.device("cpu"), seed=seed)):
+            arrays[f"case{c}_w{l}"] = w.numpy()
+        meta.append({"dims": list(dims), "seed": seed})
+    arrays["meta"] = np.array(json.dumps({"cases": meta, "generator": "reference init_weights"}))
+    np.savez_compressed(HERE / f"{name}.npz", **arrays)
+    print(name, len(arrays) - 1, "weight tensors")
+
+
 def main():
     torch.set_num_threads(1)
+    run_init("init_weights", [((10, 64, 64, 784), 0), ((10, 64, 64, 64, 64, 64, 64, 784), 3), ((10, 16, 24), 7)])
     # configs[0] of the baseline: dims (10,64,64,784), tanh, alpha 1e-4, gamma 0.5, T=4
     # (batch reduced from 128 to 8 to keep the fixture small; 2 training steps).
     run_case("c1_dims_b8", (10, 64, 64, 784), 8, "tanh", 1e-4, 0.5, 4, 2, 1, seed=11)

@@ -11,7 +11,19 @@ GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
 def cases():
-    return sorted(p.stem for p in GOLDEN.glob("*.npz"))
+    """The training-step fixtures (the weight-init fixture ``init_weights.npz`` has its own reader)."""
+    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("init_"))
+
+
+def load_init():
+    """[(dims, seed, [W_0 .. W_{L-1}])] from ``init_weights.npz`` (the reference's ``init_weights``)."""
+    z = np.load(GOLDEN / "init_weights.npz")
+    meta = json.loads(str(z["meta"]))
+    out = []
+    for c, m in enumerate(meta["cases"]):
+        L = len(m["dims"]) - 1
+        out.append((tuple(m["dims"]), m["seed"], [torch.from_numpy(z[f"case{c}_w{l}"].copy()) for l in range(L)]))
+    return out
 
 
 def load(name: str):

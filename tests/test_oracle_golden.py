@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from oracle import ipc_oracle as O
-from tests.golden_io import cases, load
+from tests.golden_io import cases, load, load_init
 
 
 @pytest.mark.parametrize("name", cases())
@@ -61,3 +61,12 @@ def test_kernel_ops_reduce_to_whole_step():
         assert O.rel_inf(wn[l], w_ref[l]) < 1e-6
     for l in range(1, L):
         assert O.rel_inf(xn[l], x_ref[l]) < 1e-6
+
+
+def test_oracle_init_matches_reference_init():
+    """oracle.init_weights draws the reference's init_weights values (CPU generator, same seeds)."""
+    for dims, seed, ref in load_init():
+        got = O.init_weights(dims, dtype=torch.float32, device="cpu", seed=seed)
+        assert len(got) == len(ref)
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b), (dims, seed)

@@ -1,0 +1,148 @@
+"""Oracle parity at the wide configurations' own sizes.
+
+* configs[4] (dims (1000, 4096 x 6, 4096), bf16, tanh, alpha 1e-4, gamma 0.5,
+  T = 4) for one training step on a column slice of the batch (B = 256; the
+  step is column-independent except for the weight update's sum over the
+  batch, so a slice is the same computation on fewer columns).  x and W are
+  gated at 1e-2 against the fp32 oracle (reference ``reference.py:42-59``);
+  the weight delta is taken in fp32 before it meets the bf16 weights (the
+  data-parallel path forms it explicitly) and gated at 1e-2 against the
+  oracle's delta ``alpha * e[l] f(x[l+1])^T`` -- at alpha 1e-4 the bf16
+  rounding of W would otherwise hide it.
+* the tensor-core kernel's P / I / W / dW modes at M = K = 4096 and 8192 with
+  B = 8192 (configs[2]'s large points), checked on sampled blocks of 256 rows
+  x 256 columns against the float64 operator oracle (full reductions).
+"""
+import pytest
+import torch
+
+from oracle import ipc_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+C5_DIMS = (1000,) + (4096,) * 6 + (4096,)
+ALPHA, GAMMA, T = 1e-4, 0.5, 4
+
+
+def _c5_inputs(B, seed):
+    from lich_b200 import synthetic as S
+    w0 = S.fan_in_normal(C5_DIMS, seed=seed)
+    (x, y), = S.batch_pool(C5_DIMS[-1], C5_DIMS[0], B, count=1, seed=seed + 1)
+    dt = torch.bfloat16
+    return [w.to(dt) for w in w0], x.to(dt), y.to(dt)
+
+
+def _oracle_delta(x, e, l):
+    """alpha * e[l] f(x[l+1])^T in float64 from the oracle's last-iteration errors and updated states."""
+    return ALPHA * (e[l].double() @ O.act_forward("tanh", x[l + 1].double()).T)
+
+
+@pytest.fixture(scope="module")
+def c5_oracle():
+    wq, x, y = _c5_inputs(256, seed=71)
+    xo, wo, eo, _ = O.train_step(x.float(), y.float(), [w.float() for w in wq], act="tanh", alpha=ALPHA,
+                                 gamma=GAMMA, T=T)
+    return wq, x, y, xo, wo, eo
+
+
+def test_c5_dims_training_step_matches_oracle(c5_oracle):
+    """TileLangIPC.train_step at configs[4] dims (operator path: tcgen05 GEMMs on the activation cache)."""
+    from lich_b200 import _native as N
+    from lich_b200.trainer import IPCConfig, TileLangIPC
+    wq, x, y, xo, wo, eo = c5_oracle
+    m = TileLangIPC(IPCConfig(dims=C5_DIMS, alpha=ALPHA, gamma=GAMMA, activation="tanh", dtype=torch.bfloat16),
+                    device=DEV)
+    assert not m.net_kernel_eligible(256)
+    for dst, src in zip(m.w, wq):
+        dst.copy_(src.to(DEV))
+    m.train_step(x.to(DEV), y.to(DEV), T=T)
+    torch.cuda.synchronize()
+    assert N.device_status() == 0
+    for l in range(len(wq)):
+        assert O.rel_inf(m.w[l].cpu(), wo[l]) <= 1e-2, ("w", l)
+    for l in range(len(C5_DIMS)):
+        assert O.rel_inf(m.x[l].cpu(), xo[l]) <= 1e-2, ("x", l)
+
+
+def test_c5_dims_fp32_weight_delta_matches_oracle(c5_oracle):
+    """The data-parallel step (one rank) keeps the fp32 delta of every layer: gate it at 1e-2 against the
+    oracle's delta at the configuration's alpha, and the applied bf16 weights at 1e-2."""
+    from lich_b200.data_parallel import DataParallelIPC
+    from lich_b200.trainer import IPCConfig
+    wq, x, y, xo, wo, eo = c5_oracle
+    dp = DataParallelIPC(IPCConfig(dims=C5_DIMS, alpha=ALPHA, gamma=GAMMA, activation="tanh",
+                                   dtype=torch.bfloat16), device=DEV)
+    for dst, src in zip(dp.model.w, wq):
+        dst.copy_(src.to(DEV))
+    dp.train_step(x.to(DEV), y.to(DEV), T=T)
+    torch.cuda.synchronize()
+    for l in range(len(wq)):
+        ref = _oracle_delta(xo, eo, l)
+        got = dp._dw[l].cpu().double()
+        if ref.abs().max().item() == 0.0:  # layers the T = 4 iterations have not reached yet
+            assert got.abs().max().item() <= 1e-6, ("dW", l)
+        else:
+            assert O.rel_inf(got, ref) <= 1e-2, ("dW", l)
+        assert O.rel_inf(dp.model.w[l].cpu(), wo[l]) <= 1e-2, ("w", l)
+
+
+def _blocks(n, k, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randperm(n, generator=g)[:k].sort().values
+
+
+def _operands(M, K, B, dt, seed):
+    from lich_b200 import synthetic as S
+    ops = S.microbench_operands(M, K, B, seed=seed, dtype=dt)
+    g = torch.Generator().manual_seed(seed + 7)
+    ops["e_lo"] = (torch.randn((M, B), generator=g) * 0.5).to(dt)
+    return ops
+
+
+@pytest.mark.parametrize("MK", [4096, 8192])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_tcgen05_large_points_sampled_blocks(MK, dt):
+    """P (saved activation), I (with A_out), W and dW at M = K = MK, B = 8192 on the tcgen05 kernel;
+    256 sampled output rows x 256 sampled columns against the float64 operator oracle."""
+    from lich_b200 import _native as N
+    M = K = MK
+    B = 8192
+    ops = _operands(M, K, B, dt, seed=MK)
+    a_up = O.act_forward("tanh", ops["x_up"].double()).to(dt)  # a saved activation f(x_up)
+    rows, cols = _blocks(M, 256, 1), _blocks(B, 256, 2)
+    kcols = _blocks(K, 256, 3)
+    d = {k: v.to(DEV) for k, v in ops.items()}
+    d["a_up"] = a_up.to(DEV)
+
+    # P: E = cast(X_lo) - cast(W @ A)
+    e = torch.empty((M, B), device=DEV, dtype=dt)
+    N.fused_gemm(N.MODE_PRED, d["w"], d["a_up"], e, d["x_lo"], M=M, K=K, B=B, act="tanh", dtype=dt, algo="tcgen05")
+    ref = O.pred_err_op(a_up[:, cols], ops["w"][rows], ops["x_lo"][rows][:, cols], act="identity", sdt=dt)
+    assert O.rel_inf(e.cpu()[rows][:, cols], ref) <= 1e-2
+
+    # I: X += gamma (-E + f'(X) W_low^T E_low), A_out = f(cast(X_new))
+    x = d["x_lo"].clone()
+    a_out = torch.empty_like(x)
+    N.fused_gemm(N.MODE_INFER, d["w_low"], d["e_low"], x, d["e_lo"], a_out, M=M, K=K, B=B, scale=GAMMA,
+                 flags=N.FLAG_AOUT_STORED, act="tanh", dtype=dt, algo="tcgen05")
+    x_ref, _ = O.infer_update_op(ops["x_lo"][rows][:, cols], ops["e_lo"][rows][:, cols], ops["w_low"][:, rows],
+                                 ops["e_low"][:, cols], act="tanh", gamma=GAMMA, sdt=dt)
+    assert O.rel_inf(x.cpu()[rows][:, cols], x_ref) <= 1e-2
+    assert O.rel_inf(a_out.cpu()[rows][:, cols], O.act_forward("tanh", x_ref.double()).to(dt)) <= 1e-2
+
+    # W: W = cast(W + alpha E A^T) (reduction over the 8192 batch columns), alpha large enough to show
+    alpha = 1e-3
+    w = d["w"].clone()
+    N.fused_gemm(N.MODE_WEIGHT, d["e_lo"], d["a_up"], w, M=M, K=K, B=B, scale=alpha, dtype=dt, algo="tcgen05")
+    w_ref = O.weight_update_op(ops["w"][rows][:, kcols], ops["e_lo"][rows], a_up[kcols], act="identity",
+                               alpha=alpha, sdt=dt, recompute_activation=False)
+    assert O.rel_inf(w.cpu()[rows][:, kcols], w_ref) <= 1e-2
+
+    # dW in fp32 at the configurations' alpha
+    dw = torch.empty((M, K), device=DEV, dtype=torch.float32)
+    N.fused_gemm(N.MODE_WDELTA, d["e_lo"], d["a_up"], dw, M=M, K=K, B=B, scale=ALPHA, dtype=dt, algo="tcgen05")
+    dw_ref = O.weight_delta_op(ops["e_lo"][rows], a_up[kcols], act="identity", alpha=ALPHA, sdt=dt,
+                               recompute_activation=False)
+    assert O.rel_inf(dw.cpu()[rows][:, kcols], dw_ref) <= 1e-3
+    torch.cuda.synchronize()
+    assert N.device_status() == 0
