@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define IPC_ABI_VERSION 2
+#define IPC_ABI_VERSION 3
 
 /* return codes */
 #define IPC_OK 0
@@ -143,9 +143,9 @@ int ipc_forward(const void* x_up, const void* w, void* out, int M, int K, int B,
  * flags: IPC_FLAG_ACTIVATE_B applies f to b (otherwise b is a saved activation);
  * IPC_FLAG_AOUT_STORED makes A_out = f(cast(x_new)), the value the recompute
  * mode reads back (default f(x_new), tilelang_kernels.py:231);
- * IPC_FLAG_ACCUMULATE adds into dw.  The tcgen05 kernel serves calls without
- * IPC_FLAG_ACTIVATE_B.  No single reference counterpart: it subsumes the
- * entries above.
+ * IPC_FLAG_ACCUMULATE adds into dw.  Without a workspace the tcgen05 kernel
+ * serves calls without IPC_FLAG_ACTIVATE_B only (with it, ipc_fused_gemm_ws
+ * below).  No single reference counterpart: it subsumes the entries above.
  */
 #define IPC_MODE_PRED 0
 #define IPC_MODE_INFER 1
@@ -166,14 +166,35 @@ int ipc_fused_gemm(int mode, const void* a, const void* b, void* out, const void
  * writes an fp32 partial tile into the workspace and a second pass sums the
  * partials in split order (deterministic) and applies the epilogue.  The
  * number of splits is bounded by workspace_bytes / (groups*M*K*4), so any
- * size works; 0 bytes is exactly ipc_fused_gemm.  Other modes ignore the
- * workspace.  Calls sharing a workspace must be ordered on one stream.  No
- * reference counterpart: the reference's weight kernel reduces the batch
- * inside one CTA per output tile (tilelang_kernels.py:269-320).
+ * size works; 0 bytes is exactly ipc_fused_gemm.  Calls sharing a workspace
+ * must be ordered on one stream.
+ * With IPC_FLAG_ACTIVATE_B (P, FORWARD, WEIGHT, WDELTA) and a tensor-core
+ * shape, the head of the workspace (groups*K*B 16-bit elements, rounded up to
+ * 256 bytes) first receives A = cast(f(b)) in one elementwise pass, and the
+ * tcgen05 GEMM runs on that stored activation; the rest of the workspace
+ * serves the split-K partials.  This is the path of the reference's
+ * recompute-mode operators (build_prediction_error, tilelang_kernels.py:
+ * 143-167; build_weight_update(recompute_activation=True), :288-321), which
+ * apply f to the B tile inside the GEMM: on tensor cores that would evaluate f
+ * once per 128-row output tile (M/128 times per element).  A workspace too
+ * small for the activation leaves such a call on the generic kernel, which
+ * applies f while staging its tiles.  ipc_fused_gemm_ws_bytes gives the size.
+ * No reference counterpart for the split: the reference's weight kernel
+ * reduces the batch inside one CTA per output tile (tilelang_kernels.py:
+ * 269-320).
  */
 int ipc_fused_gemm_ws(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K,
                       int B, int groups, float scale, int flags, int act, int dtype, int algo, void* workspace,
                       size_t workspace_bytes, void* stream);
+/* Split-K partials: this many bytes cover every weight update the kernel splits. */
+#define IPC_SPLITK_WS_BYTES (16u << 20)
+/* Workspace bytes ipc_fused_gemm_ws uses for this call (*bytes = 0: it needs
+ * none): the stored activation when IPC_FLAG_ACTIVATE_B meets a tensor-core
+ * shape, plus IPC_SPLITK_WS_BYTES for a tensor-core weight update.  Launches
+ * nothing; the answer depends only on the arguments and the current device.
+ * No reference counterpart (cf. a library's workspace-size query). */
+int ipc_fused_gemm_ws_bytes(int mode, int M, int K, int B, int groups, int flags, int dtype, int algo,
+                            size_t* bytes);
 
 /*
  * Split-K weight update that allocates nothing: ipc_fused_gemm_ws for

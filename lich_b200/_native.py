@@ -46,6 +46,7 @@ EXPORTED = (
     "ipc_forward", "ipc_infer_update", "ipc_weight_update", "ipc_weight_delta", "ipc_weight_apply",
     "ipc_activate", "ipc_net_train", "ipc_net_plan", "ipc_fused_gemm", "ipc_device_status",
     "ipc_fused_gemm_ws", "ipc_weight_update_noalloc", "ipc_selftest_barrier_timeout", "ipc_set_max_ctas",
+    "ipc_fused_gemm_ws_bytes",
 )
 
 
@@ -125,6 +126,7 @@ def load() -> ctypes.CDLL:
         "ipc_weight_update_noalloc": (i, [i, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp]),
         "ipc_selftest_barrier_timeout": (i, [vp, i, vp]),
         "ipc_set_max_ctas": (i, [i]),
+        "ipc_fused_gemm_ws_bytes": (i, [i, i, i, i, i, i, i, i, POINTER(c_size_t)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -205,6 +207,15 @@ def fused_gemm(mode: int, a, b, out, aux=None, aux2=None, *, M: int, K: int, B: 
                                        int(B), int(groups), float(scale), int(flags), act_code(act),
                                        dtype_code(dtype), ALGO_CODES[algo], ptr(workspace), nbytes,
                                        stream_handle(device)))
+
+
+def workspace_bytes(mode: int, *, M: int, K: int, B: int, groups: int = 1, flags: int = 0, dtype=torch.float16,
+                    algo: str = "auto") -> int:
+    """Workspace ``fused_gemm(..., workspace=)`` uses for this call (``ipc_fused_gemm_ws_bytes``)."""
+    n = c_size_t(0)
+    check(load().ipc_fused_gemm_ws_bytes(int(mode), int(M), int(K), int(B), int(groups), int(flags),
+                                         dtype_code(dtype), ALGO_CODES[algo], ctypes.byref(n)))
+    return int(n.value)
 
 
 def device_status(clear: bool = True) -> int:

@@ -199,6 +199,12 @@ int ipc_activate(void* a, const void* x, long long n, int act, int dtype, void* 
   return launch_activate(a, x, n, act, dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 
+// Bytes of workspace the stored activation A = cast(f(B)) of a [groups][K][B] 16-bit operand takes (a
+// multiple of 256, so the split-K partials behind it stay aligned).
+static size_t activation_ws_bytes(int groups, int K, int B) {
+  return ((size_t)groups * K * B * 2 + 255) / 256 * 256;
+}
+
 static int fused_gemm_impl(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K,
                            int B, int groups, float scale, int flags, int act, int dtype, int algo, float* ws,
                            size_t ws_bytes, void* stream) {
@@ -236,7 +242,22 @@ static int fused_gemm_impl(int mode, const void* a, const void* b, void* out, co
     p.aux = aux; p.gsAux = (long long)M * B;
     p.aux2 = aux2; p.gsAux2 = (long long)M * B;
   }
-  const bool splitk = ws != nullptr && (mode == MODE_W || mode == MODE_WD);
+  const bool weight = (mode == MODE_W || mode == MODE_WD);
+  if (bact && ws != nullptr) {
+    // f on the B operand: materialise A = cast(f(B)) once into the head of the workspace, then run the
+    // tensor-core GEMM on the stored activation (the rest of the workspace holds split-K partials).
+    // Inside the GEMM f would be evaluated once per 128-row output tile, M/128 times per element.
+    const size_t act_bytes = activation_ws_bytes(groups, K, B);
+    const bool stored_ok = tc_eligible(mode, M, K, B, dtype, algo, false, weight && ws_bytes > act_bytes);
+    if (stored_ok && ws_bytes >= act_bytes && (reinterpret_cast<uintptr_t>(b) & 15) == 0) {
+      rc = launch_activate(ws, b, (long long)groups * K * B, act, dtype, s);
+      if (rc) return rc;
+      p.Bm = ws;
+      float* part = ws_bytes > act_bytes ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + act_bytes) : nullptr;
+      return launch_tc(p, mode, act, dtype, s, part, part ? ws_bytes - act_bytes : 0);
+    }
+  }
+  const bool splitk = ws != nullptr && weight;
   if (tc_eligible(mode, M, K, B, dtype, algo, bact, splitk)) return launch_tc(p, mode, act, dtype, s, ws, ws_bytes);
   if (algo == IPC_ALGO_TCGEN05)
     return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: not eligible (mode=%d M=%d K=%d B=%d dtype=%d activate_b=%d)",
@@ -249,6 +270,25 @@ int ipc_fused_gemm(int mode, const void* a, const void* b, void* out, const void
                    int groups, float scale, int flags, int act, int dtype, int algo, void* stream) {
   return fused_gemm_impl(mode, a, b, out, aux, aux2, M, K, B, groups, scale, flags, act, dtype, algo, nullptr, 0,
                          stream);
+}
+
+int ipc_fused_gemm_ws_bytes(int mode, int M, int K, int B, int groups, int flags, int dtype, int algo,
+                            size_t* bytes) {
+  int rc = common_checks(M, K, B, groups, IPC_ACT_IDENTITY, dtype, algo);
+  if (rc) return rc;
+  IPC_REQUIRE(mode >= MODE_P && mode <= MODE_F, "unknown mode %d", mode);
+  IPC_REQUIRE(bytes != nullptr, "null result pointer");
+  const bool weight = (mode == MODE_W || mode == MODE_WD);
+  const bool bact = (flags & IPC_FLAG_ACTIVATE_B) != 0 && mode != MODE_I;
+  size_t need = 0;
+  if (!weight || algo == IPC_ALGO_OUTER || (algo == IPC_ALGO_AUTO && B <= 16)) {
+    if (bact && !weight && tc_eligible(mode, M, K, B, dtype, algo, false, false))
+      need = activation_ws_bytes(groups, K, B);
+  } else if (tc_eligible(mode, M, K, B, dtype, algo, false, true)) {
+    need = (bact ? activation_ws_bytes(groups, K, B) : 0) + IPC_SPLITK_WS_BYTES;
+  }
+  *bytes = need;
+  return IPC_OK;
 }
 
 int ipc_fused_gemm_ws(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K,

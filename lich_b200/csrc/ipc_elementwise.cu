@@ -118,6 +118,32 @@ __global__ void activate_kernel(T* __restrict__ a, const T* __restrict__ x, long
     a[i] = St<T>::st(act_f<ACT>(St<T>::ld(x[i])));
 }
 
+// 16-bit storage, both pointers 16-byte aligned: 8 elements per 16-byte access, two accesses in flight per
+// thread, f in its MUFU form (the form the tensor-core epilogues use; the result is rounded to 16 bits).
+// HBM-bound: 4 bytes of traffic per element.
+template <typename T, int ACT>
+__global__ void __launch_bounds__(256) activate16_kernel(T* __restrict__ a, const T* __restrict__ x, long long n) {
+  const long long n8 = n / 8;
+  const uint4* src = reinterpret_cast<const uint4*>(x);
+  uint4* dst = reinterpret_cast<uint4*>(a);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += 2 * stride) {
+    const bool two = i + stride < n8;
+    uint4 v0 = src[i], v1 = two ? src[i + stride] : make_uint4(0, 0, 0, 0);
+    T* h0 = reinterpret_cast<T*>(&v0);
+    T* h1 = reinterpret_cast<T*>(&v1);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      h0[j] = St<T>::st(act_f_hw<ACT>(St<T>::ld(h0[j])));
+      h1[j] = St<T>::st(act_f_hw<ACT>(St<T>::ld(h1[j])));
+    }
+    dst[i] = v0;
+    if (two) dst[i + stride] = v1;
+  }
+  for (long long i = n8 * 8 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += stride)
+    a[i] = St<T>::st(act_f_hw<ACT>(St<T>::ld(x[i])));
+}
+
 template <typename T>
 __global__ void apply_kernel(T* __restrict__ w, const float* __restrict__ dw, long long n) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
@@ -162,8 +188,17 @@ int launch_outer(void* out, const void* e, const void* x, int M, int K, int B, i
 
 int launch_activate(void* a, const void* x, long long n, int act, int dtype, cudaStream_t s) {
   if (n <= 0) return IPC_OK;
+  const bool vec = dtype != IPC_DT_F32 &&
+                   ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(x)) & 15) == 0;
   IPC_DISPATCH_DT(dtype, TT, {
     IPC_DISPATCH_ACT(act, AC, {
+      if constexpr (sizeof(TT) == 2) {
+        if (vec) {
+          activate16_kernel<TT, AC><<<148 * 8, 256, 0, s>>>(reinterpret_cast<TT*>(a), reinterpret_cast<const TT*>(x),
+                                                            n);
+          break;
+        }
+      }
       activate_kernel<TT, AC><<<grid_1d(n), 256, 0, s>>>(reinterpret_cast<TT*>(a), reinterpret_cast<const TT*>(x), n);
     });
   });

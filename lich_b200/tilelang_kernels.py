@@ -6,7 +6,10 @@ returns a cached callable specialised for ``(M, K, B, activation, dtype,
 cfg, ...)`` that mutates its tensor arguments in place on the current CUDA
 stream.  The callables run hand-written sm_100a kernels through the C ABI in
 ``include/ipc_b200.h``; nothing is JIT-compiled at build time, so a builder
-returns immediately.
+returns immediately.  On tensor-core shapes an operator with f on its B operand
+(prediction error, forward, recompute-mode weight update) first stores
+``cast(f(B))`` once into a workspace it allocates on its first call on a
+device, then runs the tcgen05 GEMM on it (``ipc_fused_gemm_ws``).
 
 Errors follow the reference: an unknown activation or dtype raises
 ``ValueError`` at build time; calling a kernel with tensors of the wrong
@@ -69,6 +72,20 @@ class _FusedOp:
         self.algo = _algo(cfg)
         self.groups = int(groups)
         self.shapes = [((self.groups,) + tuple(s)) if self.groups > 1 else tuple(s) for s in shapes]
+        self._ws: dict = {}
+
+    def _workspace(self, dev: torch.device, mode: int, flags: int):
+        """This operator's workspace for the current stream of ``dev`` (allocated on its first call there),
+        or None when the call needs none.  With f on the B operand of a tensor-core shape it holds the
+        stored activation ``cast(f(B))`` the GEMM reads (plus split-K partials for a weight update).  One
+        workspace per stream: calls of one (cached) operator on two streams may overlap."""
+        key = (dev, N.stream_handle(dev), mode, flags)
+        if key not in self._ws:
+            with torch.cuda.device(dev):
+                n = N.workspace_bytes(mode, M=self.M, K=self.K, B=self.B, groups=self.groups, flags=flags,
+                                      dtype=self.torch_dtype, algo=str(getattr(self.cfg, "backend", "auto")).lower())
+            self._ws[key] = torch.empty((n + 15) // 16 * 4, device=dev, dtype=torch.float32) if n > 0 else None
+        return self._ws[key]
 
     def _check(self, tensors):
         if len(tensors) != len(self.shapes):
@@ -91,6 +108,9 @@ class _FusedOp:
                 raise ValueError(f"{self.kind}: tensors on different devices")
         return dev
 
+    def _algo_name(self) -> str:
+        return str(getattr(self.cfg, "backend", "auto")).lower()
+
     def get_kernel_source(self) -> str:
         return (f"lich_b200 {self.kind} M/K/B shapes={self.shapes} act={self.activation} dtype={self.torch_dtype} "
                 f"backend={getattr(self.cfg, 'backend', 'auto')} (prebuilt sm_100a kernel, include/ipc_b200.h)")
@@ -108,6 +128,13 @@ class PredictionErrorKernel(_FusedOp):
         dev = self._check((x_upper, w, x_lower, e))
         s = N.stream_handle(dev)
         lib = N.load()
+        flags = 0 if self.saved else N.FLAG_ACTIVATE_B
+        ws = self._workspace(dev, N.MODE_PRED, flags)
+        if ws is not None:  # tensor-core shape: f(X_upper) stored once, then the tcgen05 GEMM
+            N.fused_gemm(N.MODE_PRED, w, x_upper, e, x_lower, M=self.M, K=self.K, B=self.B, groups=self.groups,
+                         flags=flags, act=self.activation, dtype=self.torch_dtype, algo=self._algo_name(),
+                         device=dev, workspace=ws)
+            return
         if self.saved:
             rc = lib.ipc_pred_err_saved(N.ptr(x_upper), N.ptr(w), N.ptr(x_lower), N.ptr(e), self.M, self.K, self.B,
                                         self.groups, self.dt, self.algo, s)
@@ -148,6 +175,13 @@ class WeightUpdateKernel(_FusedOp):
 
     def __call__(self, w, e, x_or_a_upper):
         dev = self._check((w, e, x_or_a_upper))
+        flags = N.FLAG_ACTIVATE_B if self.recompute else 0
+        ws = self._workspace(dev, N.MODE_WEIGHT, flags)
+        if ws is not None:  # tensor-core shape: stored activation and / or split-K partials in the workspace
+            N.fused_gemm(N.MODE_WEIGHT, e, x_or_a_upper, w, M=self.M, K=self.K, B=self.B, groups=self.groups,
+                         scale=self.alpha, flags=flags, act=self.activation, dtype=self.torch_dtype,
+                         algo=self._algo_name(), device=dev, workspace=ws)
+            return
         N.check(N.load().ipc_weight_update(N.ptr(w), N.ptr(e), N.ptr(x_or_a_upper), self.M, self.K, self.B,
                                            self.groups, self.alpha, int(self.recompute), self.act, self.dt,
                                            self.algo, N.stream_handle(dev)))
@@ -164,6 +198,12 @@ class ForwardKernel(_FusedOp):
 
     def __call__(self, x_upper, w, out):
         dev = self._check((x_upper, w, out))
+        ws = self._workspace(dev, N.MODE_FORWARD, N.FLAG_ACTIVATE_B)
+        if ws is not None:
+            N.fused_gemm(N.MODE_FORWARD, w, x_upper, out, M=self.M, K=self.K, B=self.B, groups=self.groups,
+                         flags=N.FLAG_ACTIVATE_B, act=self.activation, dtype=self.torch_dtype,
+                         algo=self._algo_name(), device=dev, workspace=ws)
+            return
         N.check(N.load().ipc_forward(N.ptr(x_upper), N.ptr(w), N.ptr(out), self.M, self.K, self.B, self.groups,
                                      self.act, self.dt, self.algo, N.stream_handle(dev)))
 

@@ -198,3 +198,87 @@ def test_cta_cap_keeps_results():
         N.set_max_ctas(0)
     with pytest.raises(ValueError):  # IPC_ERR_ARG
         N.set_max_ctas(-1)
+
+
+def _dtname(dt):
+    return "float16" if dt == torch.float16 else "bfloat16"
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+@pytest.mark.parametrize("shape", [(256, 512, 512), (1000, 1000, 264), (128, 4096, 256), (64, 512, 264)])
+def test_builders_with_f_on_b_run_on_tensor_cores(shape, dt):
+    """The reference-facing builders with f applied to their B operand (prediction error, forward, weight
+    update in recompute mode) on tensor-core shapes: f(B) is stored once in the operator's workspace and
+    the tcgen05 GEMM runs on it -- two launches (three with a split-K reduce) -- with the oracle's
+    recompute-mode answer, and bit-identical to ipc_activate followed by the stored-operand GEMM."""
+    from lich_b200.tilelang_kernels import KernelConfig, build_forward, build_prediction_error, build_weight_update
+    N = _N()
+    M, K, B = shape
+    kc = KernelConfig()
+    x_up, w, x_lo = _r((K, B), 51, 1, dt), _r((M, K), 52, K ** -0.5, dt), _r((M, B), 53, 1, dt)
+    e_lo = _r((M, B), 54, 0.5, dt)
+    d = {k: v.to(DEV) for k, v in dict(x_up=x_up, w=w, x_lo=x_lo, e_lo=e_lo).items()}
+    a_up = torch.empty_like(d["x_up"])
+    N.check(N.load().ipc_activate(a_up.data_ptr(), d["x_up"].data_ptr(), a_up.numel(), N.act_code("tanh"),
+                                  N.dtype_code(dt), N.stream_handle(DEV)))
+    # prediction error
+    e = torch.empty_like(d["x_lo"])
+    op = build_prediction_error(M, K, B, "tanh", _dtname(dt), kc)
+    op(d["x_up"], d["w"], d["x_lo"], e)  # first call allocates the workspace
+    n0 = N.launch_count()
+    op(d["x_up"], d["w"], d["x_lo"], e)
+    assert N.launch_count() - n0 == 2
+    e2 = torch.empty_like(e)
+    N.fused_gemm(N.MODE_PRED, d["w"], a_up, e2, d["x_lo"], M=M, K=K, B=B, dtype=dt, algo="tcgen05")
+    assert torch.equal(e, e2)
+    assert O.rel_inf(e.cpu(), O.pred_err_op(x_up, w, x_lo, act="tanh", sdt=dt)) <= 1e-2
+    # forward
+    out = torch.empty_like(d["x_lo"])
+    build_forward(M, K, B, "tanh", _dtname(dt), kc)(d["x_up"], d["w"], out)
+    ref = (w.double() @ O.act_forward("tanh", x_up.double()).to(dt).double()).to(dt)
+    assert O.rel_inf(out.cpu(), ref) <= 1e-2
+    # weight update, recompute mode
+    wt = d["w"].clone()
+    wop = build_weight_update(M, K, B, "tanh", _dtname(dt), kc, 1e-2, True)
+    n0 = N.launch_count()
+    wop(wt, d["e_lo"], d["x_up"])
+    assert N.launch_count() - n0 in (2, 3)
+    w2 = d["w"].clone()
+    ws = torch.empty(N.SPLITK_WORKSPACE_BYTES // 4, device=DEV, dtype=torch.float32)
+    N.fused_gemm(N.MODE_WEIGHT, d["e_lo"], a_up, w2, M=M, K=K, B=B, scale=1e-2, dtype=dt, algo="tcgen05",
+                 workspace=ws)
+    assert torch.equal(wt, w2)
+    ref = O.weight_update_op(w, e_lo, x_up, act="tanh", alpha=1e-2, sdt=dt, recompute_activation=True)
+    assert O.rel_inf(wt.cpu(), ref) <= 1e-2
+    torch.cuda.synchronize()
+    assert N.device_status() == 0
+
+
+def test_workspace_query():
+    """ipc_fused_gemm_ws_bytes: the stored activation (rounded to 256 B) on tensor-core shapes with f on B,
+    plus the split-K partials for a weight update; nothing for shapes the generic kernels take."""
+    N = _N()
+    act = N.FLAG_ACTIVATE_B
+    assert N.workspace_bytes(N.MODE_PRED, M=512, K=512, B=512, flags=act) == 512 * 512 * 2
+    assert N.workspace_bytes(N.MODE_PRED, M=512, K=512, B=512, flags=0) == 0
+    assert N.workspace_bytes(N.MODE_PRED, M=16, K=64, B=64, flags=act) == 0
+    assert N.workspace_bytes(N.MODE_WEIGHT, M=512, K=512, B=4096, flags=act) == 512 * 4096 * 2 + (16 << 20)
+    assert N.workspace_bytes(N.MODE_WEIGHT, M=512, K=512, B=4096, flags=0) == 16 << 20
+    assert N.workspace_bytes(N.MODE_WEIGHT, M=512, K=512, B=8, flags=act) == 0  # outer-product kernel
+    assert N.workspace_bytes(N.MODE_PRED, M=512, K=512, B=512, flags=act, dtype=torch.float32) == 0
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("act", ["relu", "tanh", "sigmoid", "silu", "gelu", "identity"])
+def test_activate_matches_oracle(act, dt):
+    """ipc_activate: A = cast(f(X)) elementwise (16-bit: 16-byte vectors and a scalar tail; also a view
+    that starts mid-vector, which takes the scalar kernel)."""
+    N = _N()
+    for n, off in ((1 << 20, 0), (8 * 1000 + 5, 0), (4099, 3)):
+        x = (torch.randn(n + off, generator=torch.Generator().manual_seed(n)) * 2).to(dt)
+        xd = x.to(DEV)[off:]
+        a = torch.empty(n + off, dtype=dt, device=DEV)[off:]
+        N.check(N.load().ipc_activate(a.data_ptr(), xd.data_ptr(), n, N.act_code(act), N.dtype_code(dt),
+                                      N.stream_handle(DEV)))
+        ref = O.act_forward(act, x[off:].double()).to(dt)
+        assert O.rel_inf(a.cpu(), ref) <= (1e-5 if dt == torch.float32 else 1e-2), (n, off)

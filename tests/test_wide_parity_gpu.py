@@ -138,6 +138,23 @@ def test_tcgen05_large_points_sampled_blocks(MK, dt):
                                alpha=alpha, sdt=dt, recompute_activation=False)
     assert O.rel_inf(w.cpu()[rows][:, kcols], w_ref) <= 1e-2
 
+    # the reference-facing builders with f applied to X_up (P, and W in recompute mode): f stored once,
+    # then the tcgen05 GEMM
+    from lich_b200.tilelang_kernels import KernelConfig, build_prediction_error, build_weight_update
+    dtn = "float16" if dt == torch.float16 else "bfloat16"
+    e2 = torch.empty((M, B), device=DEV, dtype=dt)
+    build_prediction_error(M, K, B, "tanh", dtn, KernelConfig())(d["x_up"], d["w"], d["x_lo"], e2)
+    ref = O.pred_err_op(ops["x_up"][:, cols], ops["w"][rows], ops["x_lo"][rows][:, cols], act="tanh", sdt=dt)
+    assert O.rel_inf(e2.cpu()[rows][:, cols], ref) <= 1e-2
+    w2 = d["w"].clone()
+    build_weight_update(M, K, B, "tanh", dtn, KernelConfig(), alpha, True)(w2, d["e_lo"], d["x_up"])
+    w_ref = O.weight_update_op(ops["w"][rows][:, kcols], ops["e_lo"][rows], ops["x_up"][kcols], act="tanh",
+                               alpha=alpha, sdt=dt, recompute_activation=True)
+    assert O.rel_inf(w2.cpu()[rows][:, kcols], w_ref) <= 1e-2
+    del e2, w2
+    build_prediction_error.cache_clear()
+    build_weight_update.cache_clear()
+
     # dW in fp32 at the configurations' alpha
     dw = torch.empty((M, K), device=DEV, dtype=torch.float32)
     N.fused_gemm(N.MODE_WDELTA, d["e_lo"], d["a_up"], dw, M=M, K=K, B=B, scale=ALPHA, dtype=dt, algo="tcgen05")
