@@ -118,6 +118,13 @@ int ipc_weight_delta(float* dw, const void* e, const void* x_up, int M, int K, i
                      float alpha, int recompute, int accumulate, int act, int dtype, int algo,
                      void* stream);
 
+/* Accuracy of a batch on the device: *count += the number of columns b whose
+ * largest logit (first on ties) sits in row labels[b].  logits [C, B] in
+ * `dtype` (the output of the forward sweep, TileLangIPC.predict), labels int64
+ * [B], count one device int (not cleared).  The reference takes the argmax on
+ * the host after predict (scripts/train_mnist.py:80-81). */
+int ipc_count_correct(const void* logits, int C, int B, const long long* labels, int* count, int dtype,
+                      void* stream);
 /* W = cast(float(W) + dw) over n elements (the epilogue of ipc_weight_update, split off). */
 int ipc_weight_apply(void* w, const float* dw, long long n, int dtype, void* stream);
 
@@ -186,6 +193,27 @@ int ipc_fused_gemm(int mode, const void* a, const void* b, void* out, const void
 int ipc_fused_gemm_ws(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K,
                       int B, int groups, float scale, int flags, int act, int dtype, int algo, void* workspace,
                       size_t workspace_bytes, void* stream);
+/* Per-call overrides of the tensor-core kernel's launch heuristics; 0 in a field
+ * keeps the library's choice.  They change which tiles, splits and CTA count
+ * compute a result, never what is computed: the output of a weight update can
+ * differ in its last bits between split counts (another summation order).
+ * Filled from a per-shape tuning table (KernelConfig rows of the reference's
+ * tuning.py:10-108 format; a sweep on the target GPU measures them). */
+typedef struct ipc_gemm_tune {
+  int bn;       /* output tile width, 128 or 256 */
+  int splits;   /* weight modes: 1 = no split-K; >= 2 = that many batch ranges
+                   (bounded by the workspace and the batch's 64-column blocks) */
+  int raster;   /* M-tiles per raster band of the persistent tile walk */
+  int max_ctas; /* persistent CTAs (also bounded by ipc_set_max_ctas and the SMs) */
+} ipc_gemm_tune_t;
+/* ipc_fused_gemm_ws with optional overrides (tune == NULL: exactly
+ * ipc_fused_gemm_ws).  IPC_ERR_ARG for bn outside {0, 128, 256} or negative
+ * fields.  Calls the tensor-core kernel does not serve ignore tune.  No
+ * reference counterpart (the reference passes a KernelConfig to its JIT
+ * compiler, tilelang_kernels.py:114-349). */
+int ipc_fused_gemm_tuned(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M,
+                         int K, int B, int groups, float scale, int flags, int act, int dtype, int algo,
+                         void* workspace, size_t workspace_bytes, const ipc_gemm_tune_t* tune, void* stream);
 /* Split-K partials: this many bytes cover every weight update the kernel splits. */
 #define IPC_SPLITK_WS_BYTES (16u << 20)
 /* Workspace bytes ipc_fused_gemm_ws uses for this call (*bytes = 0: it needs
@@ -218,7 +246,11 @@ int ipc_fused_gemm_ws_bytes(int mode, int M, int K, int B, int groups, int flags
  *     one stream.
  *   - The first call on each device does set-up (looks up the scratch
  *     address with cudaGetSymbolAddress, with that device current); make it
- *     before any stream capture.
+ *     before any stream capture.  The address is kept for the life of the
+ *     process: after a cudaDeviceReset of that device it is stale, so do not
+ *     call this entry point on a device that was reset.
+ *   - sm_100 devices only (IPC_ERR_DEVICE elsewhere), like every entry point
+ *     of this library; a split-K weight update is all it ever runs.
  * No counterpart in the reference.
  */
 #define IPC_NOALLOC_SCRATCH_BYTES (16u << 20)
@@ -226,6 +258,36 @@ int ipc_fused_gemm_ws_bytes(int mode, int M, int K, int B, int groups, int flags
 int ipc_weight_update_noalloc(int mode, const void* e, const void* a_up, void* out, int M, int K, int B, int groups,
                               float alpha, int flags, int act, int dtype, int algo, void* stream);
 
+/*
+ * Weight update with an optimizer applied where the product meets W, so no
+ * gradient tensor is written to memory (the reference lists a fused AdamW /
+ * SGD epilogue as future work, README.md:168, PERFORMANCE_CHECKLIST.md:
+ * 103-104; no counterpart exists).  The gradient of the energy
+ * sum_l |e_l|^2 / 2 with respect to W is g = -E @ A^T (summed over the batch),
+ * A = f(x_up) when recompute != 0.  Per element of W (fp32 arithmetic, W
+ * stored in `dtype`, state in fp32 with W's layout, 16-byte aligned):
+ *   IPC_OPT_SGD   (torch.optim.SGD, dampening 0, no Nesterov; buffer starts at 0):
+ *       g += weight_decay * w;  m = momentum * m + g (if m != NULL);  w -= lr * m (or g)
+ *   IPC_OPT_ADAMW (torch.optim.AdamW; step t >= 1 counts from 1):
+ *       w *= 1 - lr * weight_decay;  m = b1 m + (1 - b1) g;  v = b2 v + (1 - b2) g^2;
+ *       w -= lr / (1 - b1^t) * m / (sqrt(v) / sqrt(1 - b2^t) + eps)
+ * IPC_OPT_SGD with momentum 0, weight_decay 0 is ipc_weight_update with
+ * alpha = lr.  Paths: tcgen05 (epilogue, or the split-K reduce pass with the
+ * workspace), the small-batch outer-product kernel; shapes neither serves
+ * need workspace_bytes >= groups*M*K*4 (an fp32 product, then the step).
+ */
+#define IPC_OPT_SGD 1
+#define IPC_OPT_ADAMW 2
+typedef struct ipc_optim {
+  int kind;
+  float lr, momentum, weight_decay, beta1, beta2, eps;
+  int step;  /* AdamW: this update's step number, >= 1 */
+  float* m;  /* SGD momentum buffer (NULL without momentum) / AdamW first moment */
+  float* v;  /* AdamW second moment */
+} ipc_optim_t;
+int ipc_weight_update_opt(void* w, const void* e, const void* x_up, int M, int K, int B, int groups,
+                          const ipc_optim_t* opt, int recompute, int act, int dtype, int algo, void* workspace,
+                          size_t workspace_bytes, void* stream);
 /* First error a device-side bounded wait recorded since the last clear
  * (IPC_OK if none; IPC_ERR_TIMEOUT when a pipeline wait gave up).  Synchronises
  * with the device; clear != 0 resets the word.  No reference counterpart. */

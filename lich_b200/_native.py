@@ -46,7 +46,7 @@ EXPORTED = (
     "ipc_forward", "ipc_infer_update", "ipc_weight_update", "ipc_weight_delta", "ipc_weight_apply",
     "ipc_activate", "ipc_net_train", "ipc_net_plan", "ipc_fused_gemm", "ipc_device_status",
     "ipc_fused_gemm_ws", "ipc_weight_update_noalloc", "ipc_selftest_barrier_timeout", "ipc_set_max_ctas",
-    "ipc_fused_gemm_ws_bytes",
+    "ipc_fused_gemm_ws_bytes", "ipc_fused_gemm_tuned", "ipc_weight_update_opt", "ipc_count_correct",
 )
 
 
@@ -83,6 +83,19 @@ class IpcNetRun(Structure):
         ("phase_ns", c_void_p),
         ("sync", c_void_p),
     ]
+
+
+OPT_KINDS = {"sgd": 1, "adamw": 2}
+
+
+class IpcOptim(Structure):
+    _fields_ = [("kind", c_int), ("lr", c_float), ("momentum", c_float), ("weight_decay", c_float),
+                ("beta1", c_float), ("beta2", c_float), ("eps", c_float), ("step", c_int),
+                ("m", c_void_p), ("v", c_void_p)]
+
+
+class IpcGemmTune(Structure):
+    _fields_ = [("bn", c_int), ("splits", c_int), ("raster", c_int), ("max_ctas", c_int)]
 
 
 class IpcError(RuntimeError):
@@ -127,6 +140,10 @@ def load() -> ctypes.CDLL:
         "ipc_selftest_barrier_timeout": (i, [vp, i, vp]),
         "ipc_set_max_ctas": (i, [i]),
         "ipc_fused_gemm_ws_bytes": (i, [i, i, i, i, i, i, i, i, POINTER(c_size_t)]),
+        "ipc_fused_gemm_tuned": (i, [i, vp, vp, vp, vp, vp, i, i, i, i, f, i, i, i, i, vp, c_size_t,
+                                     POINTER(IpcGemmTune), vp]),
+        "ipc_weight_update_opt": (i, [vp, vp, vp, i, i, i, i, POINTER(IpcOptim), i, i, i, i, vp, c_size_t, vp]),
+        "ipc_count_correct": (i, [vp, i, i, vp, vp, i, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -195,9 +212,16 @@ def net_plan(dims, B: int, nets: int = 1, cluster: int = 0) -> tuple[int, int] |
 
 def fused_gemm(mode: int, a, b, out, aux=None, aux2=None, *, M: int, K: int, B: int, groups: int = 1,
                scale: float = 0.0, flags: int = 0, act: str = "identity", dtype=torch.float16, algo: str = "auto",
-               device=None, workspace=None) -> None:
-    """``ipc_fused_gemm`` on the current stream (operand roles per mode: include/ipc_b200.h)."""
-    if workspace is None:
+               device=None, workspace=None, tune: IpcGemmTune | None = None) -> None:
+    """``ipc_fused_gemm`` on the current stream (operand roles per mode: include/ipc_b200.h); with a
+    workspace ``ipc_fused_gemm_ws``, with tuning overrides ``ipc_fused_gemm_tuned``."""
+    if tune is not None:
+        nbytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+        check(load().ipc_fused_gemm_tuned(int(mode), ptr(a), ptr(b), ptr(out), ptr(aux), ptr(aux2), int(M), int(K),
+                                          int(B), int(groups), float(scale), int(flags), act_code(act),
+                                          dtype_code(dtype), ALGO_CODES[algo], ptr(workspace), nbytes,
+                                          ctypes.byref(tune), stream_handle(device)))
+    elif workspace is None:
         check(load().ipc_fused_gemm(int(mode), ptr(a), ptr(b), ptr(out), ptr(aux), ptr(aux2), int(M), int(K), int(B),
                                     int(groups), float(scale), int(flags), act_code(act), dtype_code(dtype),
                                     ALGO_CODES[algo], stream_handle(device)))
@@ -216,6 +240,22 @@ def workspace_bytes(mode: int, *, M: int, K: int, B: int, groups: int = 1, flags
     check(load().ipc_fused_gemm_ws_bytes(int(mode), int(M), int(K), int(B), int(groups), int(flags),
                                          dtype_code(dtype), ALGO_CODES[algo], ctypes.byref(n)))
     return int(n.value)
+
+
+def weight_update_opt(w, e, x_up, *, M: int, K: int, B: int, groups: int = 1, kind: str, lr: float,
+                      momentum: float = 0.0, weight_decay: float = 0.0, betas=(0.9, 0.999), eps: float = 1e-8,
+                      step: int = 1, m=None, v=None, recompute: bool = False, act: str = "identity",
+                      dtype=torch.float16, algo: str = "auto", workspace=None, device=None) -> None:
+    """``ipc_weight_update_opt`` on the current stream: an SGD / AdamW step on W from ``E @ f(X)^T``."""
+    o = IpcOptim()
+    o.kind = OPT_KINDS[kind]
+    o.lr, o.momentum, o.weight_decay = float(lr), float(momentum), float(weight_decay)
+    o.beta1, o.beta2, o.eps, o.step = float(betas[0]), float(betas[1]), float(eps), int(step)
+    o.m, o.v = ptr(m), ptr(v)
+    nbytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(load().ipc_weight_update_opt(ptr(w), ptr(e), ptr(x_up), int(M), int(K), int(B), int(groups),
+                                       ctypes.byref(o), int(bool(recompute)), act_code(act), dtype_code(dtype),
+                                       ALGO_CODES[algo], ptr(workspace), nbytes, stream_handle(device)))
 
 
 def device_status(clear: bool = True) -> int:

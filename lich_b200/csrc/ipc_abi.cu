@@ -1,3 +1,4 @@
+#include <cmath>
 // C ABI entry points (include/ipc_b200.h): argument checks, algorithm choice,
 // error reporting.  No allocation happens here; all buffers are caller-owned.
 #include <atomic>
@@ -59,6 +60,12 @@ using namespace ipc;
   do {                         \
     if (!(cond)) return set_error(IPC_ERR_ARG, __VA_ARGS__); \
   } while (0)
+
+// Bytes of workspace the stored activation A = cast(f(B)) of a [groups][K][B] 16-bit operand takes (a
+// multiple of 256, so the split-K partials behind it stay aligned).
+static size_t activation_ws_bytes(int groups, int K, int B) {
+  return ((size_t)groups * K * B * 2 + 255) / 256 * 256;
+}
 
 static int common_checks(int M, int K, int B, int groups, int act, int dtype, int algo) {
   IPC_REQUIRE(M >= 0 && K >= 0 && B >= 0, "negative size (M=%d K=%d B=%d)", M, K, B);
@@ -181,6 +188,87 @@ int ipc_weight_delta(float* dw, const void* e, const void* x_up, int M, int K, i
   return weight_impl(dw, e, x_up, M, K, B, groups, alpha, recompute, accumulate, act, dtype, algo, stream, true);
 }
 
+int ipc_weight_update_opt(void* w, const void* e, const void* x_up, int M, int K, int B, int groups,
+                          const ipc_optim_t* opt, int recompute, int act, int dtype, int algo, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  int rc = common_checks(M, K, B, groups, act, dtype, algo);
+  if (rc) return rc;
+  IPC_REQUIRE(opt != nullptr, "null optimizer descriptor");
+  IPC_REQUIRE(opt->kind == IPC_OPT_SGD || opt->kind == IPC_OPT_ADAMW, "unknown optimizer kind %d", opt->kind);
+  IPC_REQUIRE(workspace != nullptr || workspace_bytes == 0, "workspace_bytes > 0 with a null workspace");
+  IPC_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 16 == 0, "workspace must be 16-byte aligned");
+  const bool adam = opt->kind == IPC_OPT_ADAMW;
+  IPC_REQUIRE(!adam || (opt->m && opt->v), "AdamW needs both moment buffers");
+  IPC_REQUIRE(!adam || opt->step >= 1, "AdamW step must be >= 1 (got %d)", opt->step);
+  IPC_REQUIRE(adam || opt->momentum == 0.f || opt->m, "SGD with momentum needs its buffer");
+  IPC_REQUIRE(((reinterpret_cast<uintptr_t>(opt->m) | reinterpret_cast<uintptr_t>(opt->v)) & 15) == 0,
+              "optimizer state must be 16-byte aligned");
+  if (M == 0 || K == 0 || B == 0) return IPC_OK;  // an empty batch leaves W and the state as they are
+  IPC_REQUIRE(w && e && x_up, "null operand pointer");
+  OptParams o{};
+  o.kind = opt->kind;
+  o.lr = opt->lr;
+  o.momentum = opt->momentum;
+  o.wd = opt->weight_decay;
+  o.b1 = opt->beta1;
+  o.b2 = opt->beta2;
+  o.eps = opt->eps;
+  o.m = opt->m;
+  o.v = adam ? opt->v : nullptr;
+  if (!adam && opt->momentum == 0.f) o.m = nullptr;
+  if (adam) {
+    o.step_size = (float)(opt->lr / (1.0 - std::pow((double)opt->beta1, (double)opt->step)));
+    o.rsqrt_bc2 = (float)(1.0 / std::sqrt(1.0 - std::pow((double)opt->beta2, (double)opt->step)));
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool bact = recompute != 0;
+  if (algo == IPC_ALGO_OUTER || (algo == IPC_ALGO_AUTO && B <= 16))
+    return launch_outer(w, e, x_up, M, K, B, groups, 1.f, bact, false, 0, act, dtype, s, &o);
+  GemmArgs p{};
+  p.A = e; p.lda = B; p.gsA = (long long)M * B;
+  p.Bm = x_up; p.ldb = B; p.gsB = (long long)K * B;
+  p.Mg = M; p.Ng = K; p.Kg = B; p.groups = groups;
+  p.out = w; p.gsOut = (long long)M * K;
+  p.scale = 1.f;
+  p.opt = o;
+  float* ws = static_cast<float*>(workspace);
+  size_t ws_bytes = workspace_bytes;
+  if (bact) {  // f(x_up) stored once in the head of the workspace (the tensor-core kernel reads it as is)
+    const size_t act_bytes = activation_ws_bytes(groups, K, B);
+    if (tc_eligible(MODE_WO, M, K, B, dtype, algo, false, false) && ws != nullptr && ws_bytes >= act_bytes &&
+        (reinterpret_cast<uintptr_t>(x_up) & 15) == 0) {
+      rc = launch_activate(ws, x_up, (long long)groups * K * B, act, dtype, s);
+      if (rc) return rc;
+      p.Bm = ws;
+      ws = ws_bytes > act_bytes ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + act_bytes) : nullptr;
+      ws_bytes = ws ? ws_bytes - act_bytes : 0;
+      return launch_tc(p, MODE_WO, act, dtype, s, ws, ws_bytes);
+    }
+  } else if (tc_eligible(MODE_WO, M, K, B, dtype, algo, false, ws != nullptr)) {
+    return launch_tc(p, MODE_WO, act, dtype, s, ws, ws_bytes);
+  }
+  // other shapes: the fp32 product E A^T in the workspace, then the step
+  IPC_REQUIRE(ws != nullptr && workspace_bytes >= (size_t)groups * M * K * 4,
+              "optimizer update of this shape needs workspace_bytes >= groups*M*K*4 (%lld)",
+              (long long)groups * M * K * 4);
+  p.out = workspace;
+  p.scale = 1.f;
+  p.accumulate = 0;
+  rc = launch_generic(p, MODE_WD, bact, act, dtype, s);
+  if (rc) return rc;
+  return launch_opt_apply(w, static_cast<const float*>(workspace), (long long)groups * M * K, dtype, o, s);
+}
+
+int ipc_count_correct(const void* logits, int C, int B, const long long* labels, int* count, int dtype,
+                      void* stream) {
+  int rc = common_checks(1, 1, 1, 1, IPC_ACT_IDENTITY, dtype, IPC_ALGO_AUTO);
+  if (rc) return rc;
+  IPC_REQUIRE(C >= 1 && B >= 0, "C must be >= 1 and B >= 0 (C=%d B=%d)", C, B);
+  if (B == 0) return IPC_OK;
+  IPC_REQUIRE(logits && labels && count, "null operand pointer");
+  return launch_count_correct(logits, C, B, labels, count, dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int ipc_weight_apply(void* w, const float* dw, long long n, int dtype, void* stream) {
   int rc = common_checks(1, 1, 1, 1, IPC_ACT_IDENTITY, dtype, IPC_ALGO_AUTO);
   if (rc) return rc;
@@ -199,15 +287,9 @@ int ipc_activate(void* a, const void* x, long long n, int act, int dtype, void* 
   return launch_activate(a, x, n, act, dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 
-// Bytes of workspace the stored activation A = cast(f(B)) of a [groups][K][B] 16-bit operand takes (a
-// multiple of 256, so the split-K partials behind it stay aligned).
-static size_t activation_ws_bytes(int groups, int K, int B) {
-  return ((size_t)groups * K * B * 2 + 255) / 256 * 256;
-}
-
 static int fused_gemm_impl(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K,
                            int B, int groups, float scale, int flags, int act, int dtype, int algo, float* ws,
-                           size_t ws_bytes, void* stream) {
+                           size_t ws_bytes, void* stream, const TcTune* tune = nullptr) {
   int rc = common_checks(M, K, B, groups, act, dtype, algo);
   if (rc) return rc;
   IPC_REQUIRE(mode >= MODE_P && mode <= MODE_F, "unknown mode %d", mode);
@@ -254,11 +336,12 @@ static int fused_gemm_impl(int mode, const void* a, const void* b, void* out, co
       if (rc) return rc;
       p.Bm = ws;
       float* part = ws_bytes > act_bytes ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + act_bytes) : nullptr;
-      return launch_tc(p, mode, act, dtype, s, part, part ? ws_bytes - act_bytes : 0);
+      return launch_tc(p, mode, act, dtype, s, part, part ? ws_bytes - act_bytes : 0, tune);
     }
   }
   const bool splitk = ws != nullptr && weight;
-  if (tc_eligible(mode, M, K, B, dtype, algo, bact, splitk)) return launch_tc(p, mode, act, dtype, s, ws, ws_bytes);
+  if (tc_eligible(mode, M, K, B, dtype, algo, bact, splitk))
+    return launch_tc(p, mode, act, dtype, s, ws, ws_bytes, tune);
   if (algo == IPC_ALGO_TCGEN05)
     return set_error(IPC_ERR_UNSUPPORTED, "tcgen05 path: not eligible (mode=%d M=%d K=%d B=%d dtype=%d activate_b=%d)",
                      mode, M, K, B, dtype, (int)bact);
@@ -270,6 +353,26 @@ int ipc_fused_gemm(int mode, const void* a, const void* b, void* out, const void
                    int groups, float scale, int flags, int act, int dtype, int algo, void* stream) {
   return fused_gemm_impl(mode, a, b, out, aux, aux2, M, K, B, groups, scale, flags, act, dtype, algo, nullptr, 0,
                          stream);
+}
+
+int ipc_fused_gemm_tuned(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M,
+                         int K, int B, int groups, float scale, int flags, int act, int dtype, int algo,
+                         void* workspace, size_t workspace_bytes, const ipc_gemm_tune_t* tune, void* stream) {
+  IPC_REQUIRE(workspace != nullptr || workspace_bytes == 0, "workspace_bytes > 0 with a null workspace");
+  IPC_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 16 == 0, "workspace must be 16-byte aligned");
+  TcTune t{};
+  if (tune != nullptr) {
+    IPC_REQUIRE(tune->bn == 0 || tune->bn == 128 || tune->bn == 256, "tune.bn must be 0, 128 or 256 (got %d)",
+                tune->bn);
+    IPC_REQUIRE(tune->splits >= 0 && tune->raster >= 0 && tune->max_ctas >= 0,
+                "tune.splits / raster / max_ctas must be >= 0");
+    t.bn = tune->bn;
+    t.splits = tune->splits;
+    t.raster = tune->raster;
+    t.max_ctas = tune->max_ctas;
+  }
+  return fused_gemm_impl(mode, a, b, out, aux, aux2, M, K, B, groups, scale, flags, act, dtype, algo,
+                         static_cast<float*>(workspace), workspace_bytes, stream, tune ? &t : nullptr);
 }
 
 int ipc_fused_gemm_ws_bytes(int mode, int M, int K, int B, int groups, int flags, int dtype, int algo,

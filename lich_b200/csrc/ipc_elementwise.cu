@@ -9,6 +9,7 @@
 // which forms a [B, M, K] temporary with torch.bmm; the sign here is +alpha.
 #include "ipc_common.cuh"
 #include "ipc_elementwise.cuh"
+#include "ipc_generic.cuh"
 
 namespace ipc {
 namespace {
@@ -38,7 +39,8 @@ struct Vec8 {
 template <typename T, int ACT, bool BACT, bool DELTA>
 __global__ void __launch_bounds__(OT_THREADS) outer_update_kernel(void* __restrict__ out, const T* __restrict__ E,
                                                                    const T* __restrict__ X, int M, int K, int B,
-                                                                   float alpha, int accumulate, int vec_ok) {
+                                                                   float alpha, int accumulate, int vec_ok,
+                                                                   const OptParams opt) {
   __shared__ float sE[OT_ROWS][OT_BB];
   __shared__ __align__(16) float sA[OT_BB][OT_COLS];
   const int g = blockIdx.z;
@@ -94,6 +96,14 @@ __global__ void __launch_bounds__(OT_THREADS) outer_update_kernel(void* __restri
       const int k = k0 + j;
       if (k < K) dw[k] = (accumulate ? dw[k] : 0.f) + alpha * acc[j];
     }
+  } else if (opt.kind != 0) {  // optimizer step: g = -acc, state at W's index
+    T* w = reinterpret_cast<T*>(out) + (long long)g * M * K + (long long)m * K;
+    const long long base = (long long)g * M * K + (long long)m * K;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = k0 + j;
+      if (k < K) w[k] = St<T>::st(opt_step(opt, St<T>::ld(w[k]), -acc[j], base + k));
+    }
   } else {
     T* w = reinterpret_cast<T*>(out) + (long long)g * M * K + (long long)m * K;
     if (vec_ok && k0 + 8 <= K && sizeof(T) == 2) {
@@ -144,6 +154,14 @@ __global__ void __launch_bounds__(256) activate16_kernel(T* __restrict__ a, cons
     a[i] = St<T>::st(act_f_hw<ACT>(St<T>::ld(x[i])));
 }
 
+// Optimizer step from an fp32 product already in memory: g = -dw (the workspace path of shapes the fused
+// kernels do not serve).
+template <typename T>
+__global__ void opt_apply_kernel(T* __restrict__ w, const float* __restrict__ dw, long long n, const OptParams opt) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    w[i] = St<T>::st(opt_step(opt, St<T>::ld(w[i]), -dw[i], i));
+}
+
 template <typename T>
 __global__ void apply_kernel(T* __restrict__ w, const float* __restrict__ dw, long long n) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
@@ -159,7 +177,8 @@ int grid_1d(long long n) {
 }  // namespace
 
 int launch_outer(void* out, const void* e, const void* x, int M, int K, int B, int groups, float alpha,
-                 bool bact, bool delta, int accumulate, int act, int dtype, cudaStream_t s) {
+                 bool bact, bool delta, int accumulate, int act, int dtype, cudaStream_t s, const OptParams* opt) {
+  const OptParams o = opt != nullptr ? *opt : OptParams{};
   if (M <= 0 || K <= 0 || groups <= 0) return IPC_OK;
   if (B <= 0 && !delta) return IPC_OK;  // W + alpha * (empty sum) = W; a delta still writes its zeros
   dim3 grid((K + OT_COLS - 1) / OT_COLS, (M + OT_ROWS - 1) / OT_ROWS, groups);
@@ -170,15 +189,15 @@ int launch_outer(void* out, const void* e, const void* x, int M, int K, int B, i
     const TT* X = reinterpret_cast<const TT*>(x);
     if (!bact) {
       if (delta)
-        outer_update_kernel<TT, IPC_ACT_IDENTITY, false, true><<<grid, OT_THREADS, 0, s>>>(out, E, X, M, K, B, alpha, accumulate, vec_ok);
+        outer_update_kernel<TT, IPC_ACT_IDENTITY, false, true><<<grid, OT_THREADS, 0, s>>>(out, E, X, M, K, B, alpha, accumulate, vec_ok, o);
       else
-        outer_update_kernel<TT, IPC_ACT_IDENTITY, false, false><<<grid, OT_THREADS, 0, s>>>(out, E, X, M, K, B, alpha, accumulate, vec_ok);
+        outer_update_kernel<TT, IPC_ACT_IDENTITY, false, false><<<grid, OT_THREADS, 0, s>>>(out, E, X, M, K, B, alpha, accumulate, vec_ok, o);
     } else {
       IPC_DISPATCH_ACT(act, AC, {
         if (delta)
-          outer_update_kernel<TT, AC, true, true><<<grid, OT_THREADS, 0, s>>>(out, E, X, M, K, B, alpha, accumulate, vec_ok);
+          outer_update_kernel<TT, AC, true, true><<<grid, OT_THREADS, 0, s>>>(out, E, X, M, K, B, alpha, accumulate, vec_ok, o);
         else
-          outer_update_kernel<TT, AC, true, false><<<grid, OT_THREADS, 0, s>>>(out, E, X, M, K, B, alpha, accumulate, vec_ok);
+          outer_update_kernel<TT, AC, true, false><<<grid, OT_THREADS, 0, s>>>(out, E, X, M, K, B, alpha, accumulate, vec_ok, o);
       });
     }
   });
@@ -206,6 +225,15 @@ int launch_activate(void* a, const void* x, long long n, int act, int dtype, cud
   return check_launch("activate");
 }
 
+int launch_opt_apply(void* w, const float* dw, long long n, int dtype, const OptParams& opt, cudaStream_t s) {
+  if (n <= 0) return IPC_OK;
+  IPC_DISPATCH_DT(dtype, TT, {
+    opt_apply_kernel<TT><<<grid_1d(n), 256, 0, s>>>(reinterpret_cast<TT*>(w), dw, n, opt);
+  });
+  count_launch();
+  return check_launch("optimizer step");
+}
+
 int launch_apply(void* w, const float* dw, long long n, int dtype, cudaStream_t s) {
   if (n <= 0) return IPC_OK;
   IPC_DISPATCH_DT(dtype, TT, {
@@ -213,6 +241,45 @@ int launch_apply(void* w, const float* dw, long long n, int dtype, cudaStream_t 
   });
   count_launch();
   return check_launch("weight apply");
+}
+
+}  // namespace ipc
+
+namespace ipc {
+namespace {
+
+// Correct predictions of one batch: per column b, the row of the largest logit (the first on ties, as
+// torch.argmax) against labels[b]; one thread per column (rows are B apart, so a warp's loads of one
+// row are contiguous), a block-wide count, one atomic per block.
+template <typename T>
+__global__ void __launch_bounds__(256) count_correct_kernel(const T* __restrict__ logits, int C, int B,
+                                                            const long long* __restrict__ labels, int* count) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  int hit = 0;
+  if (b < B) {
+    int best = 0;
+    float bv = St<T>::ld(logits[b]);
+    for (int c = 1; c < C; ++c) {
+      const float v = St<T>::ld(logits[(long long)c * B + b]);
+      if (v > bv) { bv = v; best = c; }
+    }
+    hit = (long long)best == labels[b];
+  }
+  const int n = __syncthreads_count(hit);
+  if (threadIdx.x == 0 && n) atomicAdd(count, n);
+}
+
+}  // namespace
+
+int launch_count_correct(const void* logits, int C, int B, const long long* labels, int* count, int dtype,
+                         cudaStream_t s) {
+  if (B <= 0) return IPC_OK;
+  IPC_DISPATCH_DT(dtype, TT, {
+    count_correct_kernel<TT><<<(B + 255) / 256, 256, 0, s>>>(reinterpret_cast<const TT*>(logits), C, B, labels,
+                                                             count);
+  });
+  count_launch();
+  return check_launch("count correct");
 }
 
 }  // namespace ipc

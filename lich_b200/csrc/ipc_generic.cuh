@@ -2,9 +2,44 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include "../../include/ipc_b200.h"
+
 namespace ipc {
 
-enum GemmMode { MODE_P = 0, MODE_I = 1, MODE_W = 2, MODE_WD = 3, MODE_F = 4 };
+enum GemmMode { MODE_P = 0, MODE_I = 1, MODE_W = 2, MODE_WD = 3, MODE_F = 4, MODE_WO = 5 };
+
+// Optimizer step applied where a weight update meets W (MODE_WO and the small-batch / split-K paths), so no
+// gradient tensor is written to memory.  The gradient of the energy sum_l |e_l|^2 / 2 with respect to W[l]
+// is g = -E A^T (summed over the batch); kind IPC_OPT_SGD with momentum 0 and weight decay 0 is therefore
+// the plain iPC update W += lr E A^T.  SGD follows torch.optim.SGD (dampening 0, no Nesterov; the
+// momentum buffer starts at zero), AdamW torch.optim.AdamW (decoupled decay, bias-corrected moments).
+struct OptParams {
+  int kind;                  // 0: none, IPC_OPT_SGD, IPC_OPT_ADAMW
+  float lr, momentum, wd;    // SGD: momentum; both: weight decay
+  float b1, b2, eps;         // AdamW
+  float step_size, rsqrt_bc2;  // AdamW: lr / (1 - b1^t), 1 / sqrt(1 - b2^t)
+  float* m;                  // SGD momentum buffer / AdamW first moment (fp32, the layout of W); may be null for
+  float* v;                  //   SGD without momentum; AdamW second moment
+};
+
+// One element: w (fp32 value of the stored weight), g its gradient, i its index into m / v.
+__device__ __forceinline__ float opt_step(const OptParams& o, float w, float g, long long i) {
+  if (o.kind == IPC_OPT_ADAMW) {
+    w *= 1.f - o.lr * o.wd;
+    const float m = o.b1 * o.m[i] + (1.f - o.b1) * g;
+    const float v = o.b2 * o.v[i] + (1.f - o.b2) * g * g;
+    o.m[i] = m;
+    o.v[i] = v;
+    return w - o.step_size * m / (sqrtf(v) * o.rsqrt_bc2 + o.eps);
+  }
+  g += o.wd * w;  // SGD
+  if (o.m != nullptr) {
+    const float b = o.momentum * o.m[i] + g;
+    o.m[i] = b;
+    g = b;
+  }
+  return w - o.lr * g;
+}
 
 // C[m,n] = sum_k A(m,k) B(k,n) per group, then a MODE epilogue on the
 // row-major [Mg, Ng] output.  Orientation (fixed by MODE):
@@ -26,6 +61,7 @@ struct GemmArgs {
   float scale;      // I: gamma   W/WD: alpha
   int accumulate;   // WD
   int a_out_from_stored;  // I: A_out = f(cast(x_new)) (what recompute mode reads back) instead of f(x_new)
+  OptParams opt;    // WO: the optimizer step applied to W
 };
 
 int launch_generic(const GemmArgs& p, int mode, bool bact, int act, int dtype, cudaStream_t s);

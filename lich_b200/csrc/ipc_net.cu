@@ -132,9 +132,27 @@ __device__ __forceinline__ void nbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void nbar_expect(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-// Bounded wait on a phase of a local mbarrier; on expiry the status word is set and the caller goes
-// on (every CTA keeps reaching every cluster barrier, so the launch still ends).
-__device__ __forceinline__ void nbar_wait(uint32_t bar, uint32_t parity) {
+// The launch's abort flag: one word at the same shared-memory offset in every CTA of the cluster.  A
+// bounded wait that expires raises it in all of them (remote stores); from then on no CTA issues
+// another bulk copy, and before leaving each CTA lets the copies already in flight towards it land
+// (bounded), so no copy reaches the shared memory of a CTA that has exited.  The outputs of such a
+// launch are undefined; the status word (ipc_device_status) says IPC_ERR_TIMEOUT.
+__device__ __forceinline__ void raise_abort(uint32_t flag, int C) {
+  for (int r = 0; r < C; ++r) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(flag), "r"(r));
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(a), "r"(1u) : "memory");
+  }
+}
+__device__ __forceinline__ bool aborted(uint32_t flag) {
+  uint32_t v;
+  asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"(flag) : "memory");
+  return v != 0;
+}
+// Bounded wait on a phase of a local mbarrier; on expiry the status word is set, the abort flag is
+// raised in every CTA and the caller goes on (every CTA keeps reaching every cluster barrier, so the
+// launch still ends).
+__device__ __forceinline__ void nbar_wait(uint32_t bar, uint32_t parity, uint32_t flag, int C) {
   long long tstart = -1;
   while (true) {
     uint32_t ok;
@@ -151,8 +169,27 @@ __device__ __forceinline__ void nbar_wait(uint32_t bar, uint32_t parity) {
     if (tstart < 0) tstart = now;
     if (now - tstart > NET_WAIT_NS) {
       atomicCAS(&g_net_status, 0, IPC_ERR_TIMEOUT);
+      raise_abort(flag, C);
       return;
     }
+  }
+}
+// After an abort: let copies still in flight towards this CTA complete their phase (at most 1 ms).
+__device__ __forceinline__ void nbar_drain(uint32_t bar, uint32_t parity) {
+  long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    long long now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    if (ok || now - t0 > 1000000LL) return;
   }
 }
 // Bulk copy of `bytes` from this CTA's shared memory to the same offset in CTA `rank`, completing
@@ -398,6 +435,7 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
   // Weight-update operands: every CTA sends its e[L-1] tile to every CTA and its e[l], f(x[l+1])
   // tiles to the owner of layer l, one bulk copy each; obar expects this CTA's share per step.
   const uint32_t obar = sbase + p.o_obar;
+  const uint32_t abort_flag = sbase + p.o_bar + 8;  // the 8 bytes behind wbar (zeroed with the rest)
   uint32_t operands = (uint32_t)(C * p.rows16[Lt] * NCOL * (int)sizeof(T));
   for (int slot = 0; slot < p.nown; ++slot) {
     const int l = cta + slot * C;
@@ -516,7 +554,7 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
       U32(p.o_mu, sw<NCOL>(r, j)) = r < dT ? bits2<T>(s0, s1) : 0u;
     }
     if (p.update_weights && step > 0 && threadIdx.x == 0) {
-      nbar_wait(wbar, (uint32_t)((step - 1) & 1));  // last step's replicas have landed
+      nbar_wait(wbar, (uint32_t)((step - 1) & 1), abort_flag, C);  // last step's replicas have landed
       nbar_expect(wbar, incoming);                  // this step's
     }
     __syncthreads();
@@ -669,7 +707,7 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
       // ---- send the weight-update operands: one bulk copy per tile and destination ----
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the state tiles, to the copy engine
       __syncthreads();
-      if (threadIdx.x == 0) {
+      if (threadIdx.x == 0 && !aborted(abort_flag)) {
         const uint32_t top = (uint32_t)(p.rows16[Lt] * NCOL * (int)sizeof(T));
         for (int cc = 0; cc < C; ++cc)  // e[L-1] -> every CTA's E_top, block cta
           bulk_to(sbase + p.o_gt + (uint32_t)cta * top, sbase + p.o_e[Lt], top, obar, (uint32_t)cc);
@@ -681,8 +719,10 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
           bulk_to(sbase + p.o_ga[slot] + (uint32_t)cta * blk, sbase + p.o_a[l + 1],
                   (uint32_t)(p.rows16[l + 1] * NCOL * (int)sizeof(T)), obar, owner);
         }
+      }
+      if (threadIdx.x == 0) {
         // (B) this CTA's update operands have arrived: every peer finished its iterations
-        nbar_wait(obar, (uint32_t)(step & 1));
+        nbar_wait(obar, (uint32_t)(step & 1), abort_flag, C);
         nbar_expect(obar, operands);  // the next step's
       }
       __syncthreads();
@@ -782,7 +822,7 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
       // reads them after the generic stores above are made visible to the async proxy)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncthreads();
-      if (threadIdx.x == 0) {
+      if (threadIdx.x == 0 && !aborted(abort_flag)) {
         for (int slot = 0; slot < p.nown; ++slot) {
           const int l = cta + slot * C;
           if (l >= Lt) break;
@@ -812,7 +852,15 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
 
   // ---- outputs: states / errors of the owned columns, weights, the trained batch ----
   if (p.update_weights) {
-    if (p.steps > 0 && threadIdx.x == 0) nbar_wait(wbar, (uint32_t)((p.steps - 1) & 1));
+    if (p.steps > 0 && threadIdx.x == 0) nbar_wait(wbar, (uint32_t)((p.steps - 1) & 1), abort_flag, C);
+    if (threadIdx.x == 0 && aborted(abort_flag)) {
+      // copies already issued towards this CTA land before it leaves (their phases may be the current or
+      // the next one; both are drained, each bounded)
+      nbar_drain(wbar, 0u);
+      nbar_drain(wbar, 1u);
+      nbar_drain(obar, 0u);
+      nbar_drain(obar, 1u);
+    }
     __syncthreads();
     cluster_sync_all();  // every replica holds every owner's new tiles; no copy is still in flight
     if (cta == 0) {

@@ -69,7 +69,7 @@ constexpr int EPI_SLOT = 2048;
 constexpr int EPI_WARP_BYTES = 2 * EPI_SLOT;
 constexpr int EPI_BYTES = TC_EPI_WARPS * EPI_WARP_BYTES;
 
-constexpr int TC_RASTER = 16;  // M-tiles per raster group: a wave covers ~16 x 9 tiles, both operands stay in L2
+constexpr int TC_RASTER = 16;  // default M-tiles per raster band: a wave covers ~16 x 9 tiles, both operands in L2
 
 struct TcParams {
   int Mg, Ng, Kg, groups;
@@ -88,6 +88,8 @@ struct TcParams {
   int splits, kps;
   float* ws;
   int staged;  // P / W / I: epilogue staged through shared memory with TMA loads and stores
+  int raster;  // M-tiles per raster band of the tile walk
+  OptParams opt;  // WO: optimizer step applied to W in the epilogue
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -186,7 +188,7 @@ __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
 }
 
 // Tile t -> (group, first row, first column).  Rows are walked in bands of
-// TC_RASTER M-tiles, all N-tiles of a band before the next band, so the CTAs of
+// p.raster M-tiles, all N-tiles of a band before the next band, so the CTAs of
 // one wave share a few A row-blocks and B column-blocks in L2.
 // With split-K the split index is the fastest-varying part of t.
 __device__ __forceinline__ void tile_coords(const TcParams& p, int t, int bn, int& g, int& m0, int& n0, int& s) {
@@ -195,10 +197,10 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int t, int bn, in
   const int tiles_mn = p.tiles_m * p.tiles_n;
   g = t / tiles_mn;
   const int r = t % tiles_mn;
-  const int band = r / (TC_RASTER * p.tiles_n);
-  const int first_m = band * TC_RASTER;
-  const int band_m = min(TC_RASTER, p.tiles_m - first_m);
-  const int within = r - band * TC_RASTER * p.tiles_n;
+  const int band = r / (p.raster * p.tiles_n);
+  const int first_m = band * p.raster;
+  const int band_m = min(p.raster, p.tiles_m - first_m);
+  const int within = r - band * p.raster * p.tiles_n;
   m0 = (first_m + within % band_m) * TC_BM;
   n0 = (within / band_m) * bn;
 }
@@ -226,7 +228,7 @@ struct Vec8 {
 };
 
 // Direct epilogue for 8 consecutive columns [n, n+8) of output row m, used by the modes without a
-// staged epilogue: WD (dw = alpha acc, or += with accumulate, fp32) and F (OUT = cast(acc) and
+// staged epilogue: WD (dw = alpha acc, or += with accumulate, fp32), WO (an optimizer step on W) and F (OUT = cast(acc) and
 // f(OUT), f in its MUFU form: one fp16 rounding step, every result is stored in 16 bits).
 template <typename T, int ACT, int MODE>
 __device__ __forceinline__ void epi8(const TcParams& p, int g, int m, int n, const float (&acc)[8]) {
@@ -242,6 +244,15 @@ __device__ __forceinline__ void epi8(const TcParams& p, int g, int m, int n, con
     }
     dw[0] = a;
     dw[1] = b;
+  } else if constexpr (MODE == MODE_WO) {
+    // optimizer step on 8 weights: g = -acc (the gradient of the energy), state in fp32 at the same index
+    T* w = reinterpret_cast<T*>(p.out) + g * p.gs_out + idx;
+    uint4 raw = *reinterpret_cast<const uint4*>(w);
+    T* h = reinterpret_cast<T*>(&raw);
+    const long long base = g * p.gs_out + idx;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = St<T>::st(opt_step(p.opt, St<T>::ld(h[j]), -acc[j], base + j));
+    *reinterpret_cast<uint4*>(w) = raw;
   } else if constexpr (MODE == MODE_F) {
     float o[8];
 #pragma unroll
@@ -704,7 +715,7 @@ int grid_cap() {
 // (deterministic).  W: W = cast(W + scale * sum); WD: dw = (accumulate ? dw : 0) + scale * sum.
 template <typename T, int MODE>
 __global__ void ws_reduce_kernel(const float* __restrict__ ws, int splits, long long n4, void* out, float scale,
-                                 int accumulate) {
+                                 int accumulate, const OptParams opt) {
   const float4* part = reinterpret_cast<const float4*>(ws);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
     float4 acc = part[i];
@@ -720,6 +731,12 @@ __global__ void ws_reduce_kernel(const float* __restrict__ ws, int splits, long 
         o.x += d.x; o.y += d.y; o.z += d.z; o.w += d.w;
       }
       *dw = o;
+    } else if constexpr (MODE == MODE_WO) {
+      T* w = reinterpret_cast<T*>(out) + 4 * i;
+      w[0] = St<T>::st(opt_step(opt, St<T>::ld(w[0]), -acc.x, 4 * i));
+      w[1] = St<T>::st(opt_step(opt, St<T>::ld(w[1]), -acc.y, 4 * i + 1));
+      w[2] = St<T>::st(opt_step(opt, St<T>::ld(w[2]), -acc.z, 4 * i + 2));
+      w[3] = St<T>::st(opt_step(opt, St<T>::ld(w[3]), -acc.w, 4 * i + 3));
     } else {
       T* w = reinterpret_cast<T*>(out) + 4 * i;
       w[0] = St<T>::st(St<T>::ld(w[0]) + scale * acc.x);
@@ -731,7 +748,7 @@ __global__ void ws_reduce_kernel(const float* __restrict__ ws, int splits, long 
 }
 
 template <typename T, int ACT, int MODE, int BN>
-int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t ws_bytes) {
+int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t ws_bytes, const TcTune* tune) {
   constexpr bool A_MN = (MODE == MODE_I);
   constexpr bool B_MN = (MODE == MODE_P || MODE == MODE_I || MODE == MODE_F);
   CUtensorMap ta, tb;
@@ -757,17 +774,21 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   p.aux2 = a.aux2; p.gs_aux2 = a.gsAux2;
   p.scale = a.scale; p.accumulate = a.accumulate;
   p.a_out_from_stored = a.a_out_from_stored;
+  p.raster = (tune != nullptr && tune->raster > 0) ? tune->raster : TC_RASTER;
+  p.opt = a.opt;
   // split-K: a weight update with fewer output tiles than half the SMs and a long batch reduction
   const int nk = (a.Kg + TC_BK - 1) / TC_BK;
   p.splits = 1;
   p.kps = nk;
   p.ws = nullptr;
-  const int cap = grid_cap();
-  if ((MODE == MODE_W || MODE == MODE_WD) && ws != nullptr && p.tiles < cap / 2 && nk >= 8 &&
+  int cap = grid_cap();
+  if (tune != nullptr && tune->max_ctas > 0 && tune->max_ctas < cap) cap = tune->max_ctas;
+  const int want = tune != nullptr ? tune->splits : 0;  // 0: heuristic, 1: never, >= 2: requested
+  if ((MODE == MODE_W || MODE == MODE_WD || MODE == MODE_WO) && ws != nullptr && want != 1 &&
+      (want >= 2 || (p.tiles < cap / 2 && nk >= 8)) &&
       a.gsOut == (long long)a.Mg * a.Ng) {  // the reduce pass walks out as one dense [groups][M][N] array
     const long long tile_bytes = (long long)a.groups * a.Mg * a.Ng * 4;
-    int splits = cap / p.tiles;  // one wave: every (tile, split) unit resident at once
-    splits = min(splits, nk / 4);
+    int splits = want >= 2 ? min(want, nk) : min(cap / p.tiles, nk / 4);  // heuristic: one wave of units
     const long long fit = (long long)(ws_bytes / (size_t)tile_bytes);
     if (fit < splits) splits = (int)fit;
     if (splits >= 2) {
@@ -802,11 +823,11 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   count_launch();
   int rc2 = check_launch("tcgen05 GEMM");
   if (rc2 || p.splits == 1) return rc2;
-  if constexpr (MODE == MODE_W || MODE == MODE_WD) {
+  if constexpr (MODE == MODE_W || MODE == MODE_WD || MODE == MODE_WO) {
     const long long n4 = (long long)a.groups * a.Mg * a.Ng / 4;
     long long blocks = (n4 + 255) / 256;
     if (blocks > 148LL * 16) blocks = 148LL * 16;
-    ws_reduce_kernel<T, MODE><<<(int)blocks, 256, 0, s>>>(ws, p.splits, n4, a.out, a.scale, a.accumulate);
+    ws_reduce_kernel<T, MODE><<<(int)blocks, 256, 0, s>>>(ws, p.splits, n4, a.out, a.scale, a.accumulate, a.opt);
     count_launch();
     return check_launch("split-K reduce");
   }
@@ -814,23 +835,26 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
 }
 
 template <typename T, int MODE, int BN>
-int dispatch_act(const GemmArgs& a, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes) {
-  if constexpr (MODE == MODE_P || MODE == MODE_W || MODE == MODE_WD) {
-    return launch_tc_t<T, IPC_ACT_IDENTITY, MODE, BN>(a, dtype, s, ws, ws_bytes);  // f only in I / F epilogues
+int dispatch_act(const GemmArgs& a, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes,
+                 const TcTune* tune) {
+  if constexpr (MODE == MODE_P || MODE == MODE_W || MODE == MODE_WD || MODE == MODE_WO) {
+    return launch_tc_t<T, IPC_ACT_IDENTITY, MODE, BN>(a, dtype, s, ws, ws_bytes, tune);  // f only in I / F epilogues
   } else {
-    IPC_DISPATCH_ACT(act, AC, { return launch_tc_t<T, AC, MODE, BN>(a, dtype, s, ws, ws_bytes); });
+    IPC_DISPATCH_ACT(act, AC, { return launch_tc_t<T, AC, MODE, BN>(a, dtype, s, ws, ws_bytes, tune); });
   }
   return IPC_OK;
 }
 
 template <typename T, int BN>
-int dispatch_mode(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes) {
+int dispatch_mode(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes,
+                  const TcTune* tune) {
   switch (mode) {
-    case MODE_P: return dispatch_act<T, MODE_P, BN>(a, act, dtype, s, ws, ws_bytes);
-    case MODE_I: return dispatch_act<T, MODE_I, BN>(a, act, dtype, s, ws, ws_bytes);
-    case MODE_W: return dispatch_act<T, MODE_W, BN>(a, act, dtype, s, ws, ws_bytes);
-    case MODE_WD: return dispatch_act<T, MODE_WD, BN>(a, act, dtype, s, ws, ws_bytes);
-    case MODE_F: return dispatch_act<T, MODE_F, BN>(a, act, dtype, s, ws, ws_bytes);
+    case MODE_P: return dispatch_act<T, MODE_P, BN>(a, act, dtype, s, ws, ws_bytes, tune);
+    case MODE_I: return dispatch_act<T, MODE_I, BN>(a, act, dtype, s, ws, ws_bytes, tune);
+    case MODE_W: return dispatch_act<T, MODE_W, BN>(a, act, dtype, s, ws, ws_bytes, tune);
+    case MODE_WD: return dispatch_act<T, MODE_WD, BN>(a, act, dtype, s, ws, ws_bytes, tune);
+    case MODE_F: return dispatch_act<T, MODE_F, BN>(a, act, dtype, s, ws, ws_bytes, tune);
+    case MODE_WO: return dispatch_act<T, MODE_WO, BN>(a, act, dtype, s, ws, ws_bytes, tune);
     default: return set_error(IPC_ERR_ARG, "bad GEMM mode %d", mode);
   }
 }
@@ -842,7 +866,7 @@ bool tc_eligible(int mode, int M, int K, int B, int dtype, int algo, bool b_acti
   if (dtype != IPC_DT_F16 && dtype != IPC_DT_BF16) return false;
   if (b_activated) return false;  // f on the B operand is materialised once by the caller
   int Mg = M, Ng = B, Kg = K;
-  const bool weight = (mode == MODE_W || mode == MODE_WD);
+  const bool weight = (mode == MODE_W || mode == MODE_WD || mode == MODE_WO);
   if (weight) { Ng = K; Kg = B; }
   if (Mg < 1 || Ng < 1 || Kg < 1) return false;
   if (M % 8 || K % 8 || B % 8) return false;  // 16-byte row strides for TMA and the epilogue vectors
@@ -857,7 +881,8 @@ bool tc_eligible(int mode, int M, int K, int B, int dtype, int algo, bool b_acti
   return true;
 }
 
-int launch_tc(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes) {
+int launch_tc(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes,
+              const TcTune* tune) {
   if (a.Mg <= 0 || a.Ng <= 0 || a.groups <= 0) return IPC_OK;
   if (a.Kg <= 0) return launch_generic(a, mode, false, act, dtype, s);  // nothing to multiply
   // TMA maps and 16-byte epilogue vectors need 16-byte aligned operands; a view that starts mid-vector
@@ -866,19 +891,26 @@ int launch_tc(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, f
                         reinterpret_cast<uintptr_t>(a.out) | reinterpret_cast<uintptr_t>(a.aux) |
                         reinterpret_cast<uintptr_t>(a.aux2);
   if (mis & 15) return launch_generic(a, mode, false, act, dtype, s);
-  // 128 x 256 tiles unless that leaves SMs idle and 128 x 128 tiles would not.  A weight update that
-  // splits its batch reduction (split-K) fills the SMs with splits instead, and the wider tile reads
-  // a third less operand data from L2 per FLOP.
-  const long long t256 = (long long)((a.Mg + TC_BM - 1) / TC_BM) * ((a.Ng + 255) / 256) * a.groups;
-  const bool splitk = (mode == MODE_W || mode == MODE_WD) && ws != nullptr && t256 < grid_cap() / 2 &&
+  // Tile width: the persistent walk takes ceil(tiles / CTAs) waves of one tile time each.  A 128 x 128
+  // tile takes about 0.81 of a 128 x 256 tile's time (measured on B200 at 4096^2 x 65536: the MMAs are
+  // bound by shared-memory operand reads, and the wide tile reads a third less per FLOP), so a tile
+  // costs ~(BN + 416) units and the estimate is waves x (BN + 416); 128 x 256 tiles on a tie.  A weight
+  // update that splits its batch reduction (split-K) fills the SMs with splits instead and keeps the
+  // wide tile.
+  const long long tm = (a.Mg + TC_BM - 1) / TC_BM;
+  const long long t256 = tm * ((a.Ng + 255) / 256) * a.groups, t128 = tm * ((a.Ng + 127) / 128) * a.groups;
+  const long long cap = grid_cap();
+  const bool splitk = (mode == MODE_W || mode == MODE_WD || mode == MODE_WO) && ws != nullptr && t256 < cap / 2 &&
                       (a.Kg + TC_BK - 1) / TC_BK >= 8 && a.gsOut == (long long)a.Mg * a.Ng &&
                       ws_bytes >= (size_t)(2LL * a.groups * a.Mg * a.Ng * 4);
-  const bool wide = a.Ng >= 256 && (t256 >= grid_cap() || splitk);
+  const long long cost256 = ((t256 + cap - 1) / cap) * (256 + 416), cost128 = ((t128 + cap - 1) / cap) * (128 + 416);
+  bool wide = a.Ng >= 256 && (cost256 <= cost128 || splitk);
+  if (tune != nullptr && (tune->bn == 128 || tune->bn == 256)) wide = tune->bn == 256;
   if (dtype == IPC_DT_F16)
-    return wide ? dispatch_mode<__half, 256>(a, mode, act, dtype, s, ws, ws_bytes)
-                : dispatch_mode<__half, 128>(a, mode, act, dtype, s, ws, ws_bytes);
-  return wide ? dispatch_mode<__nv_bfloat16, 256>(a, mode, act, dtype, s, ws, ws_bytes)
-              : dispatch_mode<__nv_bfloat16, 128>(a, mode, act, dtype, s, ws, ws_bytes);
+    return wide ? dispatch_mode<__half, 256>(a, mode, act, dtype, s, ws, ws_bytes, tune)
+                : dispatch_mode<__half, 128>(a, mode, act, dtype, s, ws, ws_bytes, tune);
+  return wide ? dispatch_mode<__nv_bfloat16, 256>(a, mode, act, dtype, s, ws, ws_bytes, tune)
+              : dispatch_mode<__nv_bfloat16, 128>(a, mode, act, dtype, s, ws, ws_bytes, tune);
 }
 
 int set_max_ctas(int max_ctas) {

@@ -91,8 +91,10 @@ class DataParallelIPC:
         d = self.cfg.dims
         B = int(m.x[0].shape[1])
         if m._ac is not None:  # cached activation: a stored operand (tensor-core kernel when wide)
+            kc = m._kernel_config("weight", d[l], d[l + 1], B)
             N.fused_gemm(N.MODE_WDELTA, m.e[l], m._ac[l + 1], dw, M=d[l], K=d[l + 1], B=B, scale=self.cfg.alpha,
-                         act=self.cfg.activation, dtype=self.cfg.dtype, device=m.device, workspace=m._splitk_ws)
+                         act=self.cfg.activation, dtype=self.cfg.dtype, algo=kc.backend, device=m.device,
+                         workspace=m._splitk_ws, tune=kc.tune())
         else:
             N.fused_gemm(N.MODE_WDELTA, m.e[l], m.x[l + 1], dw, M=d[l], K=d[l + 1], B=B, scale=self.cfg.alpha,
                          flags=N.FLAG_ACTIVATE_B, act=self.cfg.activation, dtype=self.cfg.dtype, device=m.device)

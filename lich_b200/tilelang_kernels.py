@@ -37,7 +37,9 @@ class KernelConfig:
     tables and positional constructions such as
     ``KernelConfig(64, 128, 16, 128, 2, True, 8, False)`` stay valid.
     ``backend`` selects the algorithm: ``"auto"``, ``"simt"`` (generic
-    CUDA-core / mma.sync), ``"tcgen05"`` or ``"outer"`` (weight update only).
+    CUDA-core / mma.sync), ``"tcgen05"`` or ``"outer"`` (weight update only);
+    the ``tc_*`` fields override the tcgen05 kernel's launch heuristics (tuning
+    tables measured on B200 set them, ``lich_b200.tuning``).
     """
 
     block_m: int = 128
@@ -49,6 +51,21 @@ class KernelConfig:
     swizzle_panel: int = 8
     shared_swizzle: bool = False
     backend: str = "auto"
+    # launch knobs of the tcgen05 kernel (ipc_gemm_tune_t; 0 = the library's heuristic): output tile
+    # width (128 / 256), split-K ranges of a weight update (1 = none), M-tiles per raster band, CTAs
+    tc_bn: int = 0
+    tc_splits: int = 0
+    tc_raster: int = 0
+    tc_max_ctas: int = 0
+
+    def tune(self):
+        """The ``ipc_gemm_tune_t`` of this config, or None when every knob is the heuristic's."""
+        if not (self.tc_bn or self.tc_splits or self.tc_raster or self.tc_max_ctas):
+            return None
+        t = N.IpcGemmTune()
+        t.bn, t.splits, t.raster, t.max_ctas = int(self.tc_bn), int(self.tc_splits), int(self.tc_raster), \
+            int(self.tc_max_ctas)
+        return t
 
 
 def _algo(cfg: KernelConfig) -> int:
@@ -130,10 +147,10 @@ class PredictionErrorKernel(_FusedOp):
         lib = N.load()
         flags = 0 if self.saved else N.FLAG_ACTIVATE_B
         ws = self._workspace(dev, N.MODE_PRED, flags)
-        if ws is not None:  # tensor-core shape: f(X_upper) stored once, then the tcgen05 GEMM
+        if ws is not None or self.cfg.tune() is not None:  # tensor cores: f(X_upper) stored once, then tcgen05
             N.fused_gemm(N.MODE_PRED, w, x_upper, e, x_lower, M=self.M, K=self.K, B=self.B, groups=self.groups,
                          flags=flags, act=self.activation, dtype=self.torch_dtype, algo=self._algo_name(),
-                         device=dev, workspace=ws)
+                         device=dev, workspace=ws, tune=self.cfg.tune())
             return
         if self.saved:
             rc = lib.ipc_pred_err_saved(N.ptr(x_upper), N.ptr(w), N.ptr(x_lower), N.ptr(e), self.M, self.K, self.B,
@@ -159,6 +176,12 @@ class InferenceUpdateKernel(_FusedOp):
         if not self.save_activation and a_out is not None:
             raise ValueError("inference_update: kernel built without save_activation takes 4 tensors")
         dev = self._check(tensors)
+        tune = self.cfg.tune()
+        if tune is not None:
+            N.fused_gemm(N.MODE_INFER, w_lower, e_lower, x, e, a_out, M=self.M, K=self.K, B=self.B, groups=self.groups,
+                         scale=self.gamma, act=self.activation, dtype=self.torch_dtype, algo=self._algo_name(),
+                         device=dev, tune=tune)
+            return
         N.check(N.load().ipc_infer_update(N.ptr(x), N.ptr(e), N.ptr(w_lower), N.ptr(e_lower), N.ptr(a_out),
                                           self.M, self.K, self.B, self.groups, self.gamma, self.act, self.dt,
                                           self.algo, N.stream_handle(dev)))
@@ -177,10 +200,10 @@ class WeightUpdateKernel(_FusedOp):
         dev = self._check((w, e, x_or_a_upper))
         flags = N.FLAG_ACTIVATE_B if self.recompute else 0
         ws = self._workspace(dev, N.MODE_WEIGHT, flags)
-        if ws is not None:  # tensor-core shape: stored activation and / or split-K partials in the workspace
+        if ws is not None or self.cfg.tune() is not None:  # tensor cores: stored activation / split-K partials
             N.fused_gemm(N.MODE_WEIGHT, e, x_or_a_upper, w, M=self.M, K=self.K, B=self.B, groups=self.groups,
                          scale=self.alpha, flags=flags, act=self.activation, dtype=self.torch_dtype,
-                         algo=self._algo_name(), device=dev, workspace=ws)
+                         algo=self._algo_name(), device=dev, workspace=ws, tune=self.cfg.tune())
             return
         N.check(N.load().ipc_weight_update(N.ptr(w), N.ptr(e), N.ptr(x_or_a_upper), self.M, self.K, self.B,
                                            self.groups, self.alpha, int(self.recompute), self.act, self.dt,
@@ -199,10 +222,10 @@ class ForwardKernel(_FusedOp):
     def __call__(self, x_upper, w, out):
         dev = self._check((x_upper, w, out))
         ws = self._workspace(dev, N.MODE_FORWARD, N.FLAG_ACTIVATE_B)
-        if ws is not None:
+        if ws is not None or self.cfg.tune() is not None:
             N.fused_gemm(N.MODE_FORWARD, w, x_upper, out, M=self.M, K=self.K, B=self.B, groups=self.groups,
                          flags=N.FLAG_ACTIVATE_B, act=self.activation, dtype=self.torch_dtype,
-                         algo=self._algo_name(), device=dev, workspace=ws)
+                         algo=self._algo_name(), device=dev, workspace=ws, tune=self.cfg.tune())
             return
         N.check(N.load().ipc_forward(N.ptr(x_upper), N.ptr(w), N.ptr(out), self.M, self.K, self.B, self.groups,
                                      self.act, self.dt, self.algo, N.stream_handle(dev)))

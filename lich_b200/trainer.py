@@ -19,14 +19,18 @@ for the "T inference iterations + 1 weight update" schedule,
 ``train_step`` / ``train_pool`` / ``run_inference``, and
 ``state_dict`` / ``load_state_dict``.
 
-The sm_86 tuning caches the reference consults (``hierarchical_policy.json``,
-``gridz_policy.json``) do not describe this hardware; the policy fields of
-``IPCConfig`` are accepted and recorded but the sm_100a kernels pick their own
-tiles, and grid.z grouping uses ``grid_z_max_layers`` directly.
+Tuning (``lich_b200.tuning``), consulted as the reference does
+(``trainer.py:180-215,268-345``): per operator shape the execution policy's
+kernel rows (``hierarchical_policy_path``, when ``hierarchical_policy_auto``),
+then ``tuning_table`` (a ``TuningTable`` or a path; ``None`` on a B200 means
+the table measured on B200 that ships with the package), then ``cfg.kernel``.
+With ``grid_z_auto`` the grid.z layer cap for a batch comes from the execution
+policy or ``grid_z_policy_path`` (default ``grid_z_max_layers``), and the
+weights are regrouped before the first step of that batch.
 """
 from __future__ import annotations
 
-from dataclasses import asdict, dataclass, field
+from dataclasses import asdict, dataclass, field, replace
 from typing import Sequence
 
 import torch
@@ -48,7 +52,7 @@ from .tilelang_kernels import (
     build_prediction_error,
     build_weight_update,
 )
-from .tuning import TuningTable
+from .tuning import ExecutionPolicy, TuningTable, default_table, lookup_grid_z_cap
 from .weight_update_specialization import SmallBWeightPolicy, SmallBWeightUpdater
 
 TARGET_CAPABILITY = (10, 0)
@@ -70,7 +74,7 @@ class IPCConfig:
     dtype: torch.dtype = torch.float16
     kernel: KernelConfig = KernelConfig()
     recompute_activation: bool = True
-    tuning_table: TuningTable | None = None
+    tuning_table: TuningTable | str | None = None
     use_grid_z: bool = True
     grid_z_max_layers: int = 2
     grid_z_auto: bool = True
@@ -85,6 +89,14 @@ class IPCConfig:
     # sm_100a additions
     use_net_kernel: bool = True
     net_cluster: int = 0
+    # optimizer of the weight update, fused where the product meets W (no gradient tensor): "sgd" with
+    # momentum = weight_decay = 0 is the reference update W += alpha E f(x)^T; "adamw" / momentum / weight
+    # decay follow torch.optim.AdamW / SGD with lr = alpha and gradient -E f(x)^T
+    optimizer: str = "sgd"
+    momentum: float = 0.0
+    weight_decay: float = 0.0
+    betas: tuple[float, float] = (0.9, 0.999)
+    eps: float = 1e-8
 
 
 class TileLangIPC:
@@ -104,6 +116,23 @@ class TileLangIPC:
         self.act = get_activation(cfg.activation)
         N.dtype_code(cfg.dtype)
         self._runtime_recompute_activation = bool(cfg.recompute_activation)
+        self._tuning = TuningTable.load(cfg.tuning_table)
+        if self._tuning is None:
+            self._tuning = default_table()
+        self._policy: ExecutionPolicy | None = None
+        if cfg.hierarchical_policy_auto:
+            try:
+                pol = ExecutionPolicy(cfg.hierarchical_policy_path)
+                self._policy = pol if pol.exists else None
+            except (OSError, ValueError):
+                self._policy = None
+        self._kcfg_cache: dict = {}
+        if str(cfg.optimizer).lower() not in N.OPT_KINDS:
+            raise ValueError(f"unknown optimizer {cfg.optimizer!r} (sgd or adamw)")
+        self._opt_state: list | None = None  # per layer (m, v) fp32, allocated at the first update
+        self._opt_steps = 0
+        self._opt_ws: torch.Tensor | None = None
+        self._grid_z_batch: int | None = None
         self._grid_z_cap = max(0, int(cfg.grid_z_max_layers))
         self._layer_groups: tuple[LayerBatchGroup, ...] = (
             find_internal_square_groups(tuple(cfg.dims), max_group_count=self._grid_z_cap)
@@ -179,10 +208,18 @@ class TileLangIPC:
     def dtype_name(self) -> str:
         return str(self.cfg.dtype).split(".")[-1]
 
+    @property
+    def fused_optimizer(self) -> bool:
+        """Whether the weight update is an optimizer step (AdamW, momentum or weight decay) rather than the
+        reference update; such models take the operator path."""
+        c = self.cfg
+        return str(c.optimizer).lower() == "adamw" or float(c.momentum) != 0.0 or float(c.weight_decay) != 0.0
+
     def net_kernel_eligible(self, batch: int | None = None) -> bool:
         """Whether ``step_initialized`` / ``train_pool`` run as one persistent-kernel launch."""
         d = self.cfg.dims
         ok = (self.cfg.use_net_kernel and self.cfg.dtype in (torch.float16, torch.bfloat16)
+              and not self.fused_optimizer
               and self.recompute_activation and 1 <= self.L <= N.NET_MAX_LAYERS)
         if not ok:
             return False
@@ -192,8 +229,67 @@ class TileLangIPC:
         return N.net_plan(d, int(batch), 1, int(self.cfg.net_cluster)) is not None
 
     def recommended_use_cuda_graph(self, batch: int | None = None, *, default: bool = False) -> bool:
-        """Graph replay pays off whenever the step is launch-bound; the net path is one launch already."""
-        return bool(default)
+        """The execution policy's choice for this network and batch, else ``default`` (the net path is one
+        launch per block of steps already)."""
+        if self._policy is None or batch is None:
+            return bool(default)
+        return bool(self._policy.selected("use_cuda_graph", bool(default), **self._policy_key(int(batch))))
+
+    # ----------------------------------------------------------------- tuning
+    def _policy_key(self, batch: int) -> dict:
+        sigs = ["sm100a-v1"] + ([self._tuning.signature()] if self._tuning is not None else [])
+        return {"dims": tuple(self.cfg.dims), "batch": int(batch), "activation": self.cfg.activation,
+                "dtype": self.cfg.dtype, "signatures": sigs}
+
+    def _kernel_config(self, kind: str, M: int, K: int, B: int) -> KernelConfig:
+        """Kernel config of one operator shape: execution-policy row, tuning-table row, or ``cfg.kernel``."""
+        key = (kind, int(M), int(K), int(B))
+        kc = self._kcfg_cache.get(key)
+        if kc is None:
+            q = dict(kind=kind, M=M, K=K, B=B, activation=self.cfg.activation, dtype=self.cfg.dtype)
+            kc = ((self._policy.lookup_kernel(**q) if self._policy is not None else None)
+                  or (self._tuning.lookup(**q) if self._tuning is not None else None) or self.cfg.kernel)
+            self._kcfg_cache[key] = kc
+        return kc
+
+    def _apply_grid_z_policy(self, batch: int) -> None:
+        """grid.z layer cap for this batch (execution policy, then the grid.z policy file); regroups the
+        weights when it changes (before the batch's buffers are built)."""
+        if not (self.cfg.use_grid_z and self.cfg.grid_z_auto) or self._grid_z_batch == int(batch):
+            return
+        self._grid_z_batch = int(batch)
+        cap = None
+        if self._policy is not None:
+            row = self._policy.lookup_execution(**self._policy_key(batch))
+            best = (row or {}).get("best") or {}
+            cap = best.get("grid_z_max_layers")
+        if cap is None:
+            try:
+                cap = lookup_grid_z_cap(self.cfg.grid_z_policy_path, device_name=torch.cuda.get_device_name(self.device),
+                                        capability=torch.cuda.get_device_capability(self.device), dims=self.cfg.dims,
+                                        batch=batch, activation=self.cfg.activation, dtype=self.cfg.dtype,
+                                        default=int(self.cfg.grid_z_max_layers))
+            except (OSError, ValueError):
+                cap = int(self.cfg.grid_z_max_layers)
+        cap = max(0, int(cap))
+        if cap != self._grid_z_cap:
+            self._regroup(cap)
+
+    def _regroup(self, cap: int) -> None:
+        """Store the square internal layers in grid.z groups of at most ``cap`` layers (values kept)."""
+        old = [w.clone() for w in self.w]
+        self._grid_z_cap = cap
+        self._layer_groups = (find_internal_square_groups(tuple(self.cfg.dims), max_group_count=cap)
+                              if cap >= 2 else ())
+        self._edge_to_group = {l: gi for gi, g in enumerate(self._layer_groups) for l in g.edge_indices}
+        self._w_grouped = [torch.stack([old[l] for l in g.edge_indices]) for g in self._layer_groups]
+        for l in range(len(old)):
+            gi = self._edge_to_group.get(l)
+            self.w[l] = old[l] if gi is None else self._w_grouped[gi][l - self._layer_groups[gi].start]
+        self.x = self.e = self.a = None
+        self._runtime_plan_key = None
+        self._net_desc = None
+        self._invalidate_steady_state_graph()
 
     def runtime_plan_ready(self) -> bool:
         return self._runtime_plan_key is not None
@@ -210,6 +306,7 @@ class TileLangIPC:
     def _ensure_buffers(self, B: int) -> None:
         if self.x is not None and self.x[0].shape[1] == B:
             return
+        self._apply_grid_z_policy(B)
         self._invalidate_steady_state_graph()
         self._net_desc = None
         dims = self.cfg.dims
@@ -261,11 +358,15 @@ class TileLangIPC:
         return (self.cfg.dtype in (torch.float16, torch.bfloat16) and self.recompute_activation
                 and not self.net_kernel_eligible(B))
 
+    _KIND = {N.MODE_PRED: "prediction", N.MODE_INFER: "inference", N.MODE_WEIGHT: "weight",
+             N.MODE_WDELTA: "weight", N.MODE_FORWARD: "forward"}
+
     def _fg(self, mode, a, b, out, aux=None, aux2=None, *, M, K, B, groups=1, scale=0.0, flags=0):
         ws = self._splitk_ws if mode in (N.MODE_WEIGHT, N.MODE_WDELTA) else None
+        kc = self._kernel_config(self._KIND[mode], M, K, B)
         N.fused_gemm(mode, a, b, out, aux, aux2, M=M, K=K, B=B, groups=groups, scale=scale, flags=flags,
-                     act=self.cfg.activation, dtype=self.cfg.dtype, algo=getattr(self.cfg.kernel, "backend", "auto"),
-                     device=self.device, workspace=ws)
+                     act=self.cfg.activation, dtype=self.cfg.dtype, algo=getattr(kc, "backend", "auto"),
+                     device=self.device, workspace=ws, tune=kc.tune())
 
     def _prepare_runtime_plan(self, batch: int) -> None:
         """Build the kernel-call plan once per (dims, batch, activation, dtype, mode)."""
@@ -275,7 +376,8 @@ class TileLangIPC:
             return
         B = int(batch)
         d = self.cfg.dims
-        act, dt, kc = self.cfg.activation, self.dtype_name, self.cfg.kernel
+        act, dt = self.cfg.activation, self.dtype_name
+        kc = self._kernel_config
         grouped = self._grouped_edge_indices()
         grouped_inf = {l for gr in self._layer_groups for l in range(gr.start + 1, gr.end + 2)}
         pred = [None] * self.L
@@ -284,33 +386,34 @@ class TileLangIPC:
         fwd = [None] * self.L
         outer_single = []
         for l in range(self.L):
-            fwd[l] = build_forward(d[l], d[l + 1], B, act, dt, kc)
+            fwd[l] = build_forward(d[l], d[l + 1], B, act, dt, kc("forward", d[l], d[l + 1], B))
             if l not in grouped:
-                pred[l] = build_prediction_error(d[l], d[l + 1], B, act, dt, kc)
+                pred[l] = build_prediction_error(d[l], d[l + 1], B, act, dt, kc("prediction", d[l], d[l + 1], B))
                 M, K = d[l], d[l + 1]
                 if self._outer_weight_enabled(M, K, B):
                     op = self._small_b_updater.make_singleton(M=M, K=K, B=B, activation=act, dtype=self.cfg.dtype)
                     if op is not None:
                         outer_single.append((l, op))
                         continue
-                wgt[l] = build_weight_update(d[l], d[l + 1], B, act, dt, kc, self.cfg.alpha,
-                                             self.recompute_activation)
+                wgt[l] = build_weight_update(d[l], d[l + 1], B, act, dt, kc("weight", d[l], d[l + 1], B),
+                                             self.cfg.alpha, self.recompute_activation)
         for l in range(1, self.L):
             if l not in grouped_inf:
-                inf[l] = build_inference_update(d[l], d[l - 1], B, act, dt, kc, self.cfg.gamma,
-                                                not self.recompute_activation)
+                inf[l] = build_inference_update(d[l], d[l - 1], B, act, dt, kc("inference", d[l], d[l - 1], B),
+                                                self.cfg.gamma, not self.recompute_activation)
         pg, ig, wg, og = [], [], [], []
         for gr in self._layer_groups:
-            pg.append(build_prediction_error_batched(gr.width, gr.width, B, gr.count, act, dt, kc))
-            ig.append(build_inference_update_batched(gr.width, gr.width, B, gr.count, act, dt, kc, self.cfg.gamma,
-                                                     not self.recompute_activation))
+            w_ = gr.width
+            pg.append(build_prediction_error_batched(w_, w_, B, gr.count, act, dt, kc("prediction", w_, w_, B)))
+            ig.append(build_inference_update_batched(w_, w_, B, gr.count, act, dt, kc("inference", w_, w_, B),
+                                                     self.cfg.gamma, not self.recompute_activation))
             outer = None
             if self._outer_weight_enabled(gr.width, gr.width, B, gr.count):
                 outer = self._small_b_updater.make_grouped(count=gr.count, M=gr.width, K=gr.width, B=B,
                                                            activation=act, dtype=self.cfg.dtype)
             og.append(outer)
             wg.append(None if outer is not None else build_weight_update_batched(
-                gr.width, gr.width, B, gr.count, act, dt, kc, self.cfg.alpha, self.recompute_activation))
+                w_, w_, B, gr.count, act, dt, kc("weight", w_, w_, B), self.cfg.alpha, self.recompute_activation))
         self._pred_singleton_kernels, self._inf_singleton_kernels = pred, inf
         self._weight_singleton_kernels, self._fwd_singleton_kernels = wgt, fwd
         self._weight_singleton_outer_ops = tuple(outer_single)
@@ -470,6 +573,9 @@ class TileLangIPC:
                 k(self.x[l], self.e[l], self.w[l - 1], self.e[l - 1], self.a[l])
 
     def _phase_w(self):
+        if self.fused_optimizer:
+            self._phase_w_optimizer()
+            return
         if self._ac is not None:
             B, d = int(self.x[0].shape[1]), self.cfg.dims
             al = self.cfg.alpha
@@ -489,6 +595,36 @@ class TileLangIPC:
             op(self.w[l], self.e[l], self.x[l + 1] if self.a is None else self.a[l + 1])
         for l, k in self._weight_singleton_ops:
             k(self.w[l], self.e[l], self.x[l + 1] if self.a is None else self.a[l + 1])
+
+    def _phase_w_optimizer(self):
+        """Weight update as an optimizer step per layer (``ipc_weight_update_opt``): the state stays in fp32
+        beside W, the step is applied where E f(x)^T meets W."""
+        d, B, c = self.cfg.dims, int(self.x[0].shape[1]), self.cfg
+        kind = str(c.optimizer).lower()
+        if self._opt_state is None:
+            adam = kind == "adamw"
+            self._opt_state = [(torch.zeros(w.shape, device=self.device, dtype=torch.float32)
+                                if (adam or c.momentum != 0.0) else None,
+                                torch.zeros(w.shape, device=self.device, dtype=torch.float32) if adam else None)
+                               for w in self.w]
+        need = max(max(d[l] * d[l + 1] * 4, (d[l + 1] * B * 2 + 255) // 256 * 256 + N.SPLITK_WORKSPACE_BYTES)
+                   for l in range(self.L))
+        if self._opt_ws is None or self._opt_ws.numel() * 4 < need:
+            self._opt_ws = torch.empty((need + 3) // 4, device=self.device, dtype=torch.float32)
+        self._opt_steps += 1
+        for l in range(self.L):
+            if self._ac is not None:
+                src, rec = self._ac[l + 1], False
+            elif self.a is not None:
+                src, rec = self.a[l + 1], False
+            else:
+                src, rec = self.x[l + 1], True
+            m, v = self._opt_state[l]
+            kc = self._kernel_config("weight", d[l], d[l + 1], B)
+            N.weight_update_opt(self.w[l], self.e[l], src, M=d[l], K=d[l + 1], B=B, kind=kind, lr=c.alpha,
+                                momentum=c.momentum, weight_decay=c.weight_decay, betas=c.betas, eps=c.eps,
+                                step=self._opt_steps, m=m, v=v, recompute=rec, act=c.activation, dtype=c.dtype,
+                                algo=kc.backend, workspace=self._opt_ws, device=self.device)
 
     def metrics(self) -> dict[str, float]:
         """``max |e[l]|`` over ``l < L`` (reference ``trainer.py:676-678``); synchronises."""
@@ -658,16 +794,45 @@ class TileLangIPC:
         for l in reversed(range(self.L)):
             out = torch.empty((self.cfg.dims[l], B), device=self.device, dtype=self.cfg.dtype)
             build_forward(self.cfg.dims[l], self.cfg.dims[l + 1], B, self.cfg.activation, self.dtype_name,
-                          self.cfg.kernel)(h, self.w[l], out)
+                          self._kernel_config("forward", self.cfg.dims[l], self.cfg.dims[l + 1], B))(h, self.w[l], out)
             h = out
         return h
 
+    @torch.no_grad()
+    def evaluate(self, x_input: torch.Tensor, labels: torch.Tensor, *,
+                 counter: torch.Tensor | None = None) -> torch.Tensor:
+        """Correct predictions of a batch, counted on the device: ``predict`` (the forward sweep), then per
+        column the argmax over the ``d_0`` outputs against ``labels`` (``ipc_count_correct``).  Returns an
+        int32 tensor of one element (``counter``, accumulated, if given) without synchronising; the
+        reference takes the argmax on the host (``scripts/train_mnist.py:80-81``)."""
+        B = int(x_input.shape[1])
+        if labels.numel() != B:
+            raise ValueError("labels must have one entry per batch column")
+        logits = self.predict(x_input)
+        cnt = counter if counter is not None else torch.zeros(1, dtype=torch.int32, device=self.device)
+        if cnt.dtype != torch.int32 or cnt.device != self.device:
+            raise ValueError("counter must be an int32 tensor on the model device")
+        lab = labels.to(self.device, torch.int64).contiguous()
+        N.check(N.load().ipc_count_correct(logits.data_ptr(), int(self.cfg.dims[0]), B, lab.data_ptr(),
+                                           cnt.data_ptr(), N.dtype_code(self.cfg.dtype),
+                                           N.stream_handle(self.device)))
+        return cnt
+
+    def accuracy(self, x_input: torch.Tensor, labels: torch.Tensor) -> float:
+        """Fraction of correct predictions of a batch (synchronises)."""
+        return int(self.evaluate(x_input, labels).item()) / max(1, int(x_input.shape[1]))
+
     # ---------------------------------------------------------- checkpoints
     def state_dict(self) -> dict:
+        opt = None
+        if self._opt_state is not None:
+            opt = {"steps": int(self._opt_steps),
+                   "m": [None if m is None else m.clone() for m, _ in self._opt_state],
+                   "v": [None if v is None else v.clone() for _, v in self._opt_state]}
         return {"dims": tuple(self.cfg.dims), "w": [w.detach().clone() for w in self.w],
-                "steps_done": int(self.steps_done),
-                "config": {k: (str(v) if k in ("dtype", "kernel", "tuning_table") else v)
-                           for k, v in asdict(self.cfg).items() if k != "tuning_table"}}
+                "steps_done": int(self.steps_done), "optimizer": opt,
+                "config": {k: (str(v) if k in ("dtype", "kernel") else v)
+                           for k, v in asdict(replace(self.cfg, tuning_table=None)).items() if k != "tuning_table"}}
 
     def load_state_dict(self, state: dict) -> None:
         if tuple(state["dims"]) != tuple(self.cfg.dims):
@@ -677,6 +842,12 @@ class TileLangIPC:
                 raise ValueError("checkpoint weight shape mismatch")
             dst.copy_(src.to(device=self.device, dtype=self.cfg.dtype))
         self.steps_done = int(state.get("steps_done", 0))
+        opt = state.get("optimizer")
+        if opt is not None:
+            self._opt_steps = int(opt["steps"])
+            self._opt_state = [(None if m is None else m.to(self.device, torch.float32).contiguous(),
+                                None if v is None else v.to(self.device, torch.float32).contiguous())
+                               for m, v in zip(opt["m"], opt["v"])]
 
 
 def prepare_batch(images: torch.Tensor, labels: torch.Tensor, *, device: torch.device, dtype: torch.dtype,

@@ -251,10 +251,9 @@ def rel_inf(got: torch.Tensor, ref: torch.Tensor) -> float:
 # sees the same rounded states as the GPU kernels do.
 # --------------------------------------------------------------------------
 
-def train_step_storage(x_input, y_target, w, *, act: str, alpha: float, gamma: float, T: int, sdt: torch.dtype):
-    """One training step (forward sweep, T x (P, I), W with the last iteration's e) in storage dtype.
-
-    Inputs are CPU tensors; returns ``(x, w, e)`` as storage-dtype tensors."""
+def inference_storage(x_input, y_target, w, *, act: str, gamma: float, T: int, sdt: torch.dtype):
+    """Forward sweep and T x (P, I) in storage dtype; returns ``(x, e)`` of the last iteration (e computed
+    before its state update, x after it -- the operands of the weight update)."""
     L = len(w)
     w = [wi.to(sdt) for wi in w]
     dims = [wi.shape[0] for wi in w] + [w[-1].shape[1]]
@@ -266,14 +265,21 @@ def train_step_storage(x_input, y_target, w, *, act: str, alpha: float, gamma: f
         x[l] = (w[l].double() @ a).to(sdt)
     x[0] = y_target.to(sdt)
     e = None
-    for t in range(T):
+    for _ in range(T):
         e = [pred_err_op(x[l + 1], w[l], x[l], act=act, sdt=sdt) for l in range(L)]
         new_x = list(x)
         for l in range(1, L):
             new_x[l], _ = infer_update_op(x[l], e[l], w[l - 1], e[l - 1], act=act, gamma=gamma, sdt=sdt)
         x = new_x
-        if t == T - 1:
-            w = [weight_update_op(w[l], e[l], x[l + 1], act=act, alpha=alpha, sdt=sdt) for l in range(L)]
+    return x, e
+
+
+def train_step_storage(x_input, y_target, w, *, act: str, alpha: float, gamma: float, T: int, sdt: torch.dtype):
+    """One training step (forward sweep, T x (P, I), W with the last iteration's e) in storage dtype.
+
+    Inputs are CPU tensors; returns ``(x, w, e)`` as storage-dtype tensors."""
+    x, e = inference_storage(x_input, y_target, w, act=act, gamma=gamma, T=T, sdt=sdt)
+    w = [weight_update_op(w[l].to(sdt), e[l], x[l + 1], act=act, alpha=alpha, sdt=sdt) for l in range(len(w))]
     return x, w, e
 
 
@@ -284,3 +290,61 @@ def train_storage(batches, w, *, act: str, alpha: float, gamma: float, T: int, s
         xi, yi = batches[(first_batch + s) % len(batches)]
         x, w, e = train_step_storage(xi, yi, w, act=act, alpha=alpha, gamma=gamma, T=T, sdt=sdt)
     return x, w, e
+
+
+# --------------------------------------------------------------------------
+# Optimizer steps on the weight update (no reference counterpart: the
+# reference lists fused SGD / AdamW epilogues as future work, README.md:168,
+# PERFORMANCE_CHECKLIST.md:103-104).  Restated from the published algorithms
+# as torch.optim documents them (SGD: dampening 0, no Nesterov, buffer
+# started at zero; AdamW: Loshchilov & Hutter, decoupled weight decay,
+# bias-corrected moments).  The gradient of the energy sum_l |e_l|^2 / 2 with
+# respect to W[l] is g = -e[l] @ f(x[l+1])^T (summed over the batch).
+# --------------------------------------------------------------------------
+
+def optim_step(w, g, state: dict, *, kind: str, lr: float, momentum: float = 0.0, weight_decay: float = 0.0,
+               betas=(0.9, 0.999), eps: float = 1e-8):
+    """One step on float64 copies; ``state`` holds ``m`` / ``v`` / ``t`` and is updated.  Returns new w."""
+    w = w.double()
+    g = g.double()
+    if kind == "adamw":
+        b1, b2 = betas
+        t = state.get("t", 0) + 1
+        m = state.get("m", torch.zeros_like(w)) * b1 + (1 - b1) * g
+        v = state.get("v", torch.zeros_like(w)) * b2 + (1 - b2) * g * g
+        state.update(t=t, m=m, v=v)
+        w = w * (1 - lr * weight_decay)
+        return w - (lr / (1 - b1 ** t)) * m / (v.sqrt() / (1 - b2 ** t) ** 0.5 + eps)
+    if kind == "sgd":
+        g = g + weight_decay * w
+        if momentum != 0.0:
+            g = state.get("m", torch.zeros_like(w)) * momentum + g
+            state["m"] = g
+        return w - lr * g
+    raise ValueError(f"unknown optimizer {kind!r}")
+
+
+def train_step_opt(x_input, y_target, w, states, *, act: str, gamma: float, T: int, **opt):
+    """One training step whose weight update is an optimizer step: forward sweep, T inference iterations,
+    then ``optim_step`` per layer with g = -e f(x_new)^T of the last iteration.  ``states``: one dict per
+    layer, updated.  Returns ``(x, w, e)``."""
+    x = forward_init(x_input, y_target, w, act)
+    e = None
+    for _ in range(T):
+        x, _, e, _ = ipc_step(x, w, act=act, alpha=0.0, gamma=gamma, update_weights=False)
+    new_w = []
+    for l in range(len(w)):
+        g = -(e[l].double() @ act_forward(act, x[l + 1].double()).T)
+        new_w.append(optim_step(w[l], g, states[l], **opt).to(w[l].dtype))
+    return x, new_w, e
+
+
+def train_step_opt_storage(x_input, y_target, w, states, *, act: str, gamma: float, T: int, sdt: torch.dtype, **opt):
+    """``train_step_opt`` with the reference kernels' storage rounding (``inference_storage``; the gradient
+    from the stored e and cast(f(x))).  Returns ``(x, w, e)`` with w in ``sdt``."""
+    x, e = inference_storage(x_input, y_target, w, act=act, gamma=gamma, T=T, sdt=sdt)
+    new_w = []
+    for l in range(len(w)):
+        g = -(e[l].double() @ _rnd(act_forward(act, x[l + 1].double()), sdt).T)
+        new_w.append(optim_step(w[l].to(sdt), g, states[l], **opt).to(sdt))
+    return x, new_w, e

@@ -184,3 +184,34 @@ def test_steady_state_single_launch_equals_step_calls():
         res.append([t.cpu() for t in m.w + m.x])
     for a, b in zip(*res):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dims,dtype", [((10, 64, 64, 784), torch.float16), ((10, 64, 64, 784), torch.float32),
+                                        ((1000, 512, 512, 1024), torch.bfloat16)])
+def test_evaluate_counts_argmax_on_device(dims, dtype):
+    """evaluate = predict + argmax over classes (first on ties) + compare, counted on the device."""
+    from lich_b200 import synthetic as S
+    from lich_b200.trainer import TileLangIPC
+    m = TileLangIPC(_cfg(dims, dtype), device=DEV, seed=11)
+    B = 300
+    (x, y), = S.batch_pool(dims[-1], dims[0], B, count=1, seed=12)
+    labels = torch.randint(0, dims[0], (B,), generator=torch.Generator().manual_seed(13))
+    xd = x.to(DEV, dtype)
+    logits = m.predict(xd)
+    ref = int((logits.float().argmax(dim=0).cpu() == labels).sum())
+    labels[:50] = logits[:, :50].float().argmax(dim=0).cpu()  # some certain hits
+    ref = int((logits.float().argmax(dim=0).cpu() == labels).sum())
+    cnt = m.evaluate(xd, labels)
+    assert int(cnt.item()) == ref >= 50
+    m.evaluate(xd, labels.to(DEV), counter=cnt)  # accumulates
+    assert int(cnt.item()) == 2 * ref
+    assert m.accuracy(xd, labels) == ref / B
+    # ties: the first maximal row wins, as torch.argmax
+    from lich_b200 import _native as N
+    tie = torch.zeros((4, 8), device=DEV, dtype=torch.float16)
+    tie[1:3] = 1.0
+    lab = torch.full((8,), 1, dtype=torch.int64, device=DEV)
+    c = torch.zeros(1, dtype=torch.int32, device=DEV)
+    N.check(N.load().ipc_count_correct(tie.data_ptr(), 4, 8, lab.data_ptr(), c.data_ptr(), N.dtype_code(torch.float16),
+                                       N.stream_handle(DEV)))
+    assert int(c.item()) == 8

@@ -70,3 +70,35 @@ def test_oracle_init_matches_reference_init():
         assert len(got) == len(ref)
         for a, b in zip(got, ref):
             assert torch.equal(a, b), (dims, seed)
+
+
+def test_optim_step_matches_torch_optim():
+    """oracle.optim_step follows torch.optim.SGD / AdamW step for step (CPU, float64)."""
+    g0 = torch.Generator().manual_seed(3)
+    w0 = torch.randn(7, 5, generator=g0, dtype=torch.float64)
+    grads = [torch.randn(7, 5, generator=g0, dtype=torch.float64) for _ in range(4)]
+    cases = [("adamw", dict(lr=1e-2, weight_decay=0.1, betas=(0.8, 0.95), eps=1e-6),
+              lambda p: torch.optim.AdamW([p], lr=1e-2, weight_decay=0.1, betas=(0.8, 0.95), eps=1e-6)),
+             ("sgd", dict(lr=5e-2, momentum=0.9, weight_decay=0.01),
+              lambda p: torch.optim.SGD([p], lr=5e-2, momentum=0.9, weight_decay=0.01)),
+             ("sgd", dict(lr=5e-2), lambda p: torch.optim.SGD([p], lr=5e-2))]
+    for kind, kw, make in cases:
+        p = torch.nn.Parameter(w0.clone())
+        opt = make(p)
+        w, state = w0.clone(), {}
+        for g in grads:
+            p.grad = g.clone()
+            opt.step()
+            w = O.optim_step(w, g, state, kind=kind, **kw)
+            assert torch.allclose(w, p.detach(), rtol=1e-12, atol=1e-12), (kind, kw)
+
+
+def test_plain_sgd_step_is_the_ipc_update():
+    """SGD without momentum or decay at lr = alpha is the reference weight update W += alpha E A^T."""
+    meta, w_in, batches, w_out, x_out = load("small_tanh")
+    xb, yb = batches[0]
+    x, w, e = O.train_step_opt(xb, yb, w_in, [{} for _ in w_in], act="tanh", gamma=meta["gamma"], T=meta["T"],
+                               kind="sgd", lr=meta["alpha"])
+    x2, w2, e2, _ = O.train_step(xb, yb, w_in, act="tanh", alpha=meta["alpha"], gamma=meta["gamma"], T=meta["T"])
+    for a, b in zip(w, w2):
+        assert O.rel_inf(a, b) <= 1e-6
