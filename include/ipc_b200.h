@@ -205,6 +205,11 @@ typedef struct ipc_gemm_tune {
                    (bounded by the workspace and the batch's 64-column blocks) */
   int raster;   /* M-tiles per raster band of the persistent tile walk */
   int max_ctas; /* persistent CTAs (also bounded by ipc_set_max_ctas and the SMs) */
+  int pair;     /* CTA pairs -- 256 x 256 tiles computed by two CTAs of a cluster with
+                   cta_group::2 MMAs (each CTA holds 128 rows of A and 128 columns of B);
+                   for tiles of width 256 that do not split the batch.  0: the launcher's
+                   choice (pairs unless row padding makes single CTAs cheaper), 1: single
+                   CTAs, 2: pairs */
 } ipc_gemm_tune_t;
 /* ipc_fused_gemm_ws with optional overrides (tune == NULL: exactly
  * ipc_fused_gemm_ws).  IPC_ERR_ARG for bn outside {0, 128, 256} or negative

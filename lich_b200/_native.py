@@ -95,7 +95,7 @@ class IpcOptim(Structure):
 
 
 class IpcGemmTune(Structure):
-    _fields_ = [("bn", c_int), ("splits", c_int), ("raster", c_int), ("max_ctas", c_int)]
+    _fields_ = [("bn", c_int), ("splits", c_int), ("raster", c_int), ("max_ctas", c_int), ("pair", c_int)]
 
 
 class IpcError(RuntimeError):

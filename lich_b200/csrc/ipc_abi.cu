@@ -366,6 +366,8 @@ int ipc_fused_gemm_tuned(int mode, const void* a, const void* b, void* out, cons
                 tune->bn);
     IPC_REQUIRE(tune->splits >= 0 && tune->raster >= 0 && tune->max_ctas >= 0,
                 "tune.splits / raster / max_ctas must be >= 0");
+    IPC_REQUIRE(tune->pair >= 0 && tune->pair <= 2, "tune.pair must be 0, 1 or 2 (got %d)", tune->pair);
+    t.pair = tune->pair;
     t.bn = tune->bn;
     t.splits = tune->splits;
     t.raster = tune->raster;

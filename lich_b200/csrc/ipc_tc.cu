@@ -58,6 +58,7 @@ namespace {
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;
 constexpr int TC_STAGES = 4;
+constexpr int TC_STAGES_PAIR = 6;  // a pair CTA's stage holds 128 rows of A and BN/2 of B: 32 KB
 constexpr int TC_EPI_WARPS = 8;                     // two per TMEM lane quarter
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;  // TMA warp + MMA warp + epilogue
 constexpr long long TC_WAIT_NS = 2000000000LL;
@@ -191,7 +192,10 @@ __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
 // p.raster M-tiles, all N-tiles of a band before the next band, so the CTAs of
 // one wave share a few A row-blocks and B column-blocks in L2.
 // With split-K the split index is the fastest-varying part of t.
-__device__ __forceinline__ void tile_coords(const TcParams& p, int t, int bn, int& g, int& m0, int& n0, int& s) {
+// tm: rows of a tile (128, or 256 for a CTA pair); rank: the CTA's half of a pair tile (its m0 is the
+// first row it owns: tile row + 128 rank).
+__device__ __forceinline__ void tile_coords(const TcParams& p, int t, int bn, int& g, int& m0, int& n0, int& s,
+                                            int tm = TC_BM, int rank = 0) {
   s = t % p.splits;
   t /= p.splits;
   const int tiles_mn = p.tiles_m * p.tiles_n;
@@ -201,8 +205,51 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int t, int bn, in
   const int first_m = band * p.raster;
   const int band_m = min(p.raster, p.tiles_m - first_m);
   const int within = r - band * p.raster * p.tiles_n;
-  m0 = (first_m + within % band_m) * TC_BM;
+  m0 = (first_m + within % band_m) * tm + TC_BM * rank;
   n0 = (within / band_m) * bn;
+}
+
+// ---- CTA-pair (cta_group::2) helpers: a 256 x BN tile computed by two CTAs of a cluster, each holding
+// 128 rows of A and BN/2 columns of B; the even CTA (the leader) issues the MMAs, the odd CTA's TMA
+// loads complete on the leader's stage barriers, the commits arrive at both CTAs' barriers.
+__device__ __forceinline__ uint32_t cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa0(uint32_t addr) {  // the same shared variable in the leader CTA
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(addr));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+// Arrive on the barrier at this offset in both CTAs of the pair once the issued MMAs are done.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)3)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
@@ -309,7 +356,7 @@ __device__ __forceinline__ void epi_load_i(const CUtensorMap* map0, const CUtens
   tma_load_3d(slot + tile_bytes, map1, bar, n, r0, g);
 }
 
-template <typename T, int ACT, int MODE, int BN>
+template <typename T, int ACT, int MODE, int BN, int PAIR>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE0, const __grid_constant__ CUtensorMap tmE1,
@@ -317,52 +364,75 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // tmE0..2: the I epilogue's operand maps (E, X, A_out)
   constexpr bool A_MN = (MODE == MODE_I);
   constexpr bool B_MN = (MODE == MODE_P || MODE == MODE_I || MODE == MODE_F);
+  constexpr int NCTA = PAIR ? 2 : 1;
+  constexpr int TM = TC_BM * NCTA;    // rows of a tile
+  constexpr int BNL = BN / NCTA;      // columns of B this CTA loads
+  constexpr int STAGES = PAIR ? TC_STAGES_PAIR : TC_STAGES;
   constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
-  constexpr uint32_t B_BYTES = BN * TC_BK * 2;
+  constexpr uint32_t B_BYTES = BNL * TC_BK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
-  // instruction descriptor: fp32 accumulate, A/B fp16 or bf16, majors, N, M = 128
+  // instruction descriptor: fp32 accumulate, A/B fp16 or bf16, majors, N, M = 128 (256 for a pair)
   constexpr uint32_t FMT = std::is_same<T, __half>::value ? 0u : 1u;
   constexpr uint32_t IDESC = (1u << 4) | (FMT << 7) | (FMT << 10) | ((A_MN ? 1u : 0u) << 15) |
-                             ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+                             ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr bool EPI_STAGED = (MODE == MODE_P || MODE == MODE_W || MODE == MODE_I);
   constexpr uint32_t EPI_REGION = EPI_STAGED ? EPI_BYTES : 0;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TC_STAGES * STAGE_BYTES + EPI_REGION);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + EPI_REGION);
   // bars: full[S], empty[S], tfull[2], tempty[2], epilogue slots[2 per epilogue warp]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * TC_STAGES + 4 + 2 * TC_EPI_WARPS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4 + 2 * TC_EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  const uint32_t full0 = saddr(bars), empty0 = saddr(bars + TC_STAGES);
-  const uint32_t tfull0 = saddr(bars + 2 * TC_STAGES), tempty0 = saddr(bars + 2 * TC_STAGES + 2);
-  const uint32_t ebar0 = saddr(bars + 2 * TC_STAGES + 4);
+  const uint32_t full0 = saddr(bars), empty0 = saddr(bars + STAGES);
+  const uint32_t tfull0 = saddr(bars + 2 * STAGES), tempty0 = saddr(bars + 2 * STAGES + 2);
+  const uint32_t ebar0 = saddr(bars + 2 * STAGES + 4);
+  // a pair: rank 0 leads (its stage barriers count both CTAs' loads, its tempty both CTAs' epilogues)
+  const int rank = PAIR ? (int)cta_rank() : 0;
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < TC_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
-      mbar_init(tempty0 + 8 * b, 32 * TC_EPI_WARPS);
+      mbar_init(tempty0 + 8 * b, 32 * TC_EPI_WARPS * NCTA);
     }
     for (int b = 0; b < 2 * TC_EPI_WARPS; ++b) mbar_init(ebar0 + 8 * b, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
-                 "r"(TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  if (warp == 1) {  // a pair allocates collectively: the same warp of both CTAs, the same columns in each
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                   "r"(TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                   "r"(TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before either signals the other's
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int nk = (p.Kg + TC_BK - 1) / TC_BK;
+  // an epilogue thread has read its part of an accumulator: arrive on the leader's tempty barrier
+  auto release_acc = [&](uint32_t bar) {
+    if constexpr (PAIR) {
+      if (rank == 0) mbar_arrive(bar); else mbar_arrive_remote(mapa0(bar));
+    } else {
+      mbar_arrive(bar);
+    }
+  };
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -373,9 +443,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int s = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+    for (int t = unit0; t < p.tiles && ok; t += units) {
       int g, m0, n0, sp;
-      tile_coords(p, t, BN, g, m0, n0, sp);
+      tile_coords(p, t, BN, g, m0, n0, sp, TM, rank);  // m0: this CTA's first row
+      const int nb = n0 + BNL * rank;                  // this CTA's first B column
       const int kb_end = min(nk, (sp + 1) * p.kps);
       for (int kb = sp * p.kps; kb < kb_end; ++kb) {
         ok = mbar_wait(empty0 + 8 * s, phase ^ 1, abort_flag);
@@ -383,32 +454,53 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (!ok) break;
         if (lane == 0) {
           const uint32_t full = full0 + 8 * s;
-          mbar_expect_tx(full, STAGE_BYTES);
           const uint32_t sa = saddr(smem + s * STAGE_BYTES), sb = sa + A_BYTES;
           const int k0 = kb * TC_BK;
-          if constexpr (A_MN) {
-            tma_load_3d(sa, &tmA, full, m0, k0, g);
-            tma_load_3d(sa + A_BYTES / 2, &tmA, full, m0 + 64, k0, g);
-          } else {
-            tma_load_3d(sa, &tmA, full, k0, m0, g);
-          }
-          if constexpr (B_MN) {
+          if constexpr (PAIR) {
+            // both CTAs' halves complete on the leader's barrier; the leader expects the pair's bytes
+            const uint32_t fl = mapa0(full);
+            if (rank == 0) mbar_expect_tx(full, 2 * STAGE_BYTES);
+            if constexpr (A_MN) {
+              tma_load_3d_pair(sa, &tmA, fl, m0, k0, g);
+              tma_load_3d_pair(sa + A_BYTES / 2, &tmA, fl, m0 + 64, k0, g);
+            } else {
+              tma_load_3d_pair(sa, &tmA, fl, k0, m0, g);
+            }
+            if constexpr (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sb + j * (64 * TC_BK * 2), &tmB, full, n0 + 64 * j, k0, g);
+              for (int j = 0; j < BNL / 64; ++j)
+                tma_load_3d_pair(sb + j * (64 * TC_BK * 2), &tmB, fl, nb + 64 * j, k0, g);
+            } else {
+              tma_load_3d_pair(sb, &tmB, fl, k0, nb, g);
+            }
           } else {
-            tma_load_3d(sb, &tmB, full, k0, n0, g);
+            mbar_expect_tx(full, STAGE_BYTES);
+            if constexpr (A_MN) {
+              tma_load_3d(sa, &tmA, full, m0, k0, g);
+              tma_load_3d(sa + A_BYTES / 2, &tmA, full, m0 + 64, k0, g);
+            } else {
+              tma_load_3d(sa, &tmA, full, k0, m0, g);
+            }
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j) tma_load_3d(sb + j * (64 * TC_BK * 2), &tmB, full, n0 + 64 * j, k0, g);
+            } else {
+              tma_load_3d(sb, &tmB, full, k0, n0, g);
+            }
           }
         }
         __syncwarp();
-        if (++s == TC_STAGES) { s = 0; phase ^= 1; }
+        if (++s == STAGES) { s = 0; phase ^= 1; }
       }
     }
   } else if (warp == 1) {
     // ------------------------------ MMA issuer -------------------------------
+    // (a pair's odd CTA issues nothing: the leader's cta_group::2 MMAs read both CTAs' stages)
+    if (rank == 0) {
     int s = 0, acc = 0;
     uint32_t phase = 0, aphase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+    for (int t = unit0; t < p.tiles && ok; t += units) {
       ok = mbar_wait(tempty0 + 8 * acc, aphase ^ 1, abort_flag);
       __syncwarp();
       if (!ok) break;
@@ -429,18 +521,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             // MN-major: +2 groups of 8 K-rows (2 KB) per step; 64-element MN blocks 8 KB apart.
             const uint64_t ad = A_MN ? smem_desc(sa + kk * 2048, 64 * TC_BK * 2, 1024) : smem_desc(sa + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? smem_desc(sb + kk * 2048, 64 * TC_BK * 2, 1024) : smem_desc(sb + kk * 32, 16, 1024);
-            tc_mma(d_tmem, ad, bd, IDESC, (kb > kb_begin || kk > 0) ? 1u : 0u);
+            if constexpr (PAIR)
+              tc_mma_pair(d_tmem, ad, bd, IDESC, (kb > kb_begin || kk > 0) ? 1u : 0u);
+            else
+              tc_mma(d_tmem, ad, bd, IDESC, (kb > kb_begin || kk > 0) ? 1u : 0u);
           }
-          tc_commit(empty0 + 8 * s);  // stage free once these MMAs have read it
+          // stage free (in both CTAs of a pair) once these MMAs have read it
+          if constexpr (PAIR) tc_commit_pair(empty0 + 8 * s); else tc_commit(empty0 + 8 * s);
         }
         __syncwarp();
-        if (++s == TC_STAGES) { s = 0; phase ^= 1; }
+        if (++s == STAGES) { s = 0; phase ^= 1; }
       }
       if (!ok) break;
-      if (lane == 0) tc_commit(tfull0 + 8 * acc);  // accumulator ready
+      if (lane == 0) {  // accumulator ready (a pair: each CTA's half of it)
+        if constexpr (PAIR) tc_commit_pair(tfull0 + 8 * acc); else tc_commit(tfull0 + 8 * acc);
+      }
       __syncwarp();
       if (++acc == 2) { acc = 0; aphase ^= 1; }
     }
+    }  // rank 0
   } else {
     // ------------------------------- epilogue --------------------------------
     const int q = warp & 3;     // TMEM lane quarter this warp may access
@@ -460,7 +559,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // with coalesced 16-byte stores (a warp instruction covers 4 rows x 128 bytes).
         constexpr int NCH = HC / 64;        // 64-column chunks per warp and tile
         constexpr int NPRE = 8 * NCH;       // prefetched 16-byte vectors per thread
-        const uint32_t xb = saddr(smem + TC_STAGES * STAGE_BYTES) + (warp - 2) * EPI_WARP_BYTES;
+        const uint32_t xb = saddr(smem + STAGES * STAGE_BYTES) + (warp - 2) * EPI_WARP_BYTES;
         const T* src = reinterpret_cast<const T*>(MODE == MODE_P ? p.aux : p.out);
         const long long gsrc = MODE == MODE_P ? p.gs_aux : p.gs_out;
         T* dst = reinterpret_cast<T*>(p.out);
@@ -468,7 +567,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         uint4 pre[NPRE];
         auto prefetch = [&](int t) {
           int g, m0, n0, sp;
-          tile_coords(p, t, BN, g, m0, n0, sp);
+          tile_coords(p, t, BN, g, m0, n0, sp, TM, rank);
           const int r0 = m0 + 32 * q, nw = n0 + c_lo;
 #pragma unroll
           for (int cc = 0; cc < NCH; ++cc) {
@@ -480,10 +579,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
           }
         };
-        if (blockIdx.x < p.tiles) prefetch(blockIdx.x);
-        for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
+        if (unit0 < p.tiles) prefetch(unit0);
+        for (int t = unit0; t < p.tiles; t += units) {
           int g, m0, n0, sp;
-          tile_coords(p, t, BN, g, m0, n0, sp);
+          tile_coords(p, t, BN, g, m0, n0, sp, TM, rank);
           const int r0 = m0 + 32 * q, nw = n0 + c_lo;
           const bool ok = mbar_wait(tfull0 + 8 * acc, aphase, abort_flag);
           __syncwarp();
@@ -498,7 +597,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               const int r = 4 * i + cr;
               sts128(xb + r * 128 + ((cj ^ (r & 7)) << 4), pre[8 * cc + i]);
             }
-            if (cc == NCH - 1 && t + (int)gridDim.x < p.tiles) prefetch(t + gridDim.x);
+            if (cc == NCH - 1 && t + units < p.tiles) prefetch(t + units);
             __syncwarp();
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
@@ -512,7 +611,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             if (cc == NCH - 1) {  // every accumulator column read: release it to the MMA warp
               tc_fence_before();
-              mbar_arrive(tempty0 + 8 * acc);
+              release_acc(tempty0 + 8 * acc);
             }
             __syncwarp();
 #pragma unroll
@@ -535,13 +634,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         constexpr int CW = 16;
         constexpr int NSUB = HC / CW;
         constexpr uint32_t TILE = 32 * CW * 2;  // one 32-row operand tile (32-byte rows)
-        const uint32_t ebase = saddr(smem + TC_STAGES * STAGE_BYTES) + (warp - 2) * EPI_WARP_BYTES;
+        const uint32_t ebase = saddr(smem + STAGES * STAGE_BYTES) + (warp - 2) * EPI_WARP_BYTES;
         const uint32_t ebar = ebar0 + 16 * (warp - 2);
         uint32_t eph = 0, pending = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+        for (int t = unit0; t < p.tiles && ok; t += units) {
           int g, m0, n0, sp;
-          tile_coords(p, t, BN, g, m0, n0, sp);
+          tile_coords(p, t, BN, g, m0, n0, sp, TM, rank);
           const int r0 = m0 + 32 * q;
           const bool live = r0 < p.Mg;
           const int nw = n0 + c_lo;
@@ -602,7 +701,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
           if (!ok) break;
           tc_fence_before();
-          mbar_arrive(tempty0 + 8 * acc);
+          release_acc(tempty0 + 8 * acc);
           if (++acc == 2) { acc = 0; aphase ^= 1; }
         }
         if (lane == 0) {
@@ -615,9 +714,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __syncwarp();
       }
     } else {
-      for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
+      for (int t = unit0; t < p.tiles; t += units) {
         int g, m0, n0, sp;
-        tile_coords(p, t, BN, g, m0, n0, sp);
+        tile_coords(p, t, BN, g, m0, n0, sp, TM, rank);
         const int m = m0 + 32 * q + lane;
         const bool ok = mbar_wait(tfull0 + 8 * acc, aphase, abort_flag);
         __syncwarp();
@@ -650,16 +749,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(tempty0 + 8 * acc);
+        release_acc(tempty0 + 8 * acc);
         if (++acc == 2) { acc = 0; aphase ^= 1; }
       }
     }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the leader's MMAs and the odd CTA's loads are done with both CTAs
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+    if constexpr (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
   }
 }
 
@@ -747,10 +850,12 @@ __global__ void ws_reduce_kernel(const float* __restrict__ ws, int splits, long 
   }
 }
 
-template <typename T, int ACT, int MODE, int BN>
+template <typename T, int ACT, int MODE, int BN, int PAIR>
 int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t ws_bytes, const TcTune* tune) {
   constexpr bool A_MN = (MODE == MODE_I);
   constexpr bool B_MN = (MODE == MODE_P || MODE == MODE_I || MODE == MODE_F);
+  constexpr int TM = PAIR ? 2 * TC_BM : TC_BM;  // rows of a tile
+  constexpr int BNL = PAIR ? BN / 2 : BN;       // B columns one CTA loads
   CUtensorMap ta, tb;
   int rc;
   // A operand: rows are the M side (K-major) or the K side (MN-major)
@@ -762,11 +867,11 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   if (B_MN)
     rc = make_map(&tb, a.Bm, dtype, a.Ng, a.Kg, a.groups, a.ldb, a.gsB, 64, TC_BK);
   else
-    rc = make_map(&tb, a.Bm, dtype, a.Kg, a.Ng, a.groups, a.ldb, a.gsB, TC_BK, BN);
+    rc = make_map(&tb, a.Bm, dtype, a.Kg, a.Ng, a.groups, a.ldb, a.gsB, TC_BK, BNL);
   if (rc) return rc;
   TcParams p{};
   p.Mg = a.Mg; p.Ng = a.Ng; p.Kg = a.Kg; p.groups = a.groups;
-  p.tiles_m = (a.Mg + TC_BM - 1) / TC_BM;
+  p.tiles_m = (a.Mg + TM - 1) / TM;
   p.tiles_n = (a.Ng + BN - 1) / BN;
   p.tiles = p.tiles_m * p.tiles_n * a.groups;
   p.out = a.out; p.ld_out = a.Ng; p.gs_out = a.gsOut;
@@ -784,7 +889,7 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   int cap = grid_cap();
   if (tune != nullptr && tune->max_ctas > 0 && tune->max_ctas < cap) cap = tune->max_ctas;
   const int want = tune != nullptr ? tune->splits : 0;  // 0: heuristic, 1: never, >= 2: requested
-  if ((MODE == MODE_W || MODE == MODE_WD || MODE == MODE_WO) && ws != nullptr && want != 1 &&
+  if ((MODE == MODE_W || MODE == MODE_WD || MODE == MODE_WO) && !PAIR && ws != nullptr && want != 1 &&
       (want >= 2 || (p.tiles < cap / 2 && nk >= 8)) &&
       a.gsOut == (long long)a.Mg * a.Ng) {  // the reduce pass walks out as one dense [groups][M][N] array
     const long long tile_bytes = (long long)a.groups * a.Mg * a.Ng * 4;
@@ -813,13 +918,35 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
       if (rc) return rc;
     }
   }
-  constexpr int STAGE_BYTES = (TC_BM + BN) * TC_BK * 2;
-  const int smem = TC_STAGES * STAGE_BYTES + (EPI_STAGED ? EPI_BYTES : 0) + 1024 + 256;
-  auto kern = tc_gemm_kernel<T, ACT, MODE, BN>;
+  constexpr int STAGE_BYTES = (TC_BM + BNL) * TC_BK * 2;
+  constexpr int STAGES = PAIR ? TC_STAGES_PAIR : TC_STAGES;
+  // barriers (2 per stage, 4 accumulator, 2 per epilogue warp), the TMEM slot and the abort word
+  constexpr int TAIL = ((2 * STAGES + 4 + 2 * TC_EPI_WARPS) * 8 + 8 + 255) / 256 * 256;
+  const int smem = STAGES * STAGE_BYTES + (EPI_STAGED ? EPI_BYTES : 0) + 1024 + TAIL;
+  auto kern = tc_gemm_kernel<T, ACT, MODE, BN, PAIR>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "tcgen05 kernel smem attribute: %s", cudaGetErrorString(err));
-  const int grid = p.tiles < cap ? p.tiles : cap;
-  kern<<<grid, TC_THREADS, smem, s>>>(ta, tb, te[0], te[1], te[2], p);
+  if constexpr (PAIR) {
+    // clusters of two CTAs, one pair per two SMs, each pair walking 256-row tiles
+    const int pairs = p.tiles < cap / 2 ? p.tiles : cap / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (pairs > 0 ? pairs : 1), 1, 1);
+    cfg.blockDim = dim3(TC_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    err = cudaLaunchKernelEx(&cfg, kern, ta, tb, te[0], te[1], te[2], p);
+    if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "tcgen05 pair GEMM launch: %s", cudaGetErrorString(err));
+  } else {
+    const int grid = p.tiles < cap ? p.tiles : cap;
+    kern<<<grid, TC_THREADS, smem, s>>>(ta, tb, te[0], te[1], te[2], p);
+  }
   count_launch();
   int rc2 = check_launch("tcgen05 GEMM");
   if (rc2 || p.splits == 1) return rc2;
@@ -834,27 +961,27 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   return IPC_OK;
 }
 
-template <typename T, int MODE, int BN>
+template <typename T, int MODE, int BN, int PAIR>
 int dispatch_act(const GemmArgs& a, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes,
                  const TcTune* tune) {
   if constexpr (MODE == MODE_P || MODE == MODE_W || MODE == MODE_WD || MODE == MODE_WO) {
-    return launch_tc_t<T, IPC_ACT_IDENTITY, MODE, BN>(a, dtype, s, ws, ws_bytes, tune);  // f only in I / F epilogues
+    return launch_tc_t<T, IPC_ACT_IDENTITY, MODE, BN, PAIR>(a, dtype, s, ws, ws_bytes, tune);  // f only in I / F
   } else {
-    IPC_DISPATCH_ACT(act, AC, { return launch_tc_t<T, AC, MODE, BN>(a, dtype, s, ws, ws_bytes, tune); });
+    IPC_DISPATCH_ACT(act, AC, { return launch_tc_t<T, AC, MODE, BN, PAIR>(a, dtype, s, ws, ws_bytes, tune); });
   }
   return IPC_OK;
 }
 
-template <typename T, int BN>
+template <typename T, int BN, int PAIR>
 int dispatch_mode(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, float* ws, size_t ws_bytes,
                   const TcTune* tune) {
   switch (mode) {
-    case MODE_P: return dispatch_act<T, MODE_P, BN>(a, act, dtype, s, ws, ws_bytes, tune);
-    case MODE_I: return dispatch_act<T, MODE_I, BN>(a, act, dtype, s, ws, ws_bytes, tune);
-    case MODE_W: return dispatch_act<T, MODE_W, BN>(a, act, dtype, s, ws, ws_bytes, tune);
-    case MODE_WD: return dispatch_act<T, MODE_WD, BN>(a, act, dtype, s, ws, ws_bytes, tune);
-    case MODE_F: return dispatch_act<T, MODE_F, BN>(a, act, dtype, s, ws, ws_bytes, tune);
-    case MODE_WO: return dispatch_act<T, MODE_WO, BN>(a, act, dtype, s, ws, ws_bytes, tune);
+    case MODE_P: return dispatch_act<T, MODE_P, BN, PAIR>(a, act, dtype, s, ws, ws_bytes, tune);
+    case MODE_I: return dispatch_act<T, MODE_I, BN, PAIR>(a, act, dtype, s, ws, ws_bytes, tune);
+    case MODE_W: return dispatch_act<T, MODE_W, BN, PAIR>(a, act, dtype, s, ws, ws_bytes, tune);
+    case MODE_WD: return dispatch_act<T, MODE_WD, BN, PAIR>(a, act, dtype, s, ws, ws_bytes, tune);
+    case MODE_F: return dispatch_act<T, MODE_F, BN, PAIR>(a, act, dtype, s, ws, ws_bytes, tune);
+    case MODE_WO: return dispatch_act<T, MODE_WO, BN, PAIR>(a, act, dtype, s, ws, ws_bytes, tune);
     default: return set_error(IPC_ERR_ARG, "bad GEMM mode %d", mode);
   }
 }
@@ -906,11 +1033,25 @@ int launch_tc(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, f
   const long long cost256 = ((t256 + cap - 1) / cap) * (256 + 416), cost128 = ((t128 + cap - 1) / cap) * (128 + 416);
   bool wide = a.Ng >= 256 && (cost256 <= cost128 || splitk);
   if (tune != nullptr && (tune->bn == 128 || tune->bn == 256)) wide = tune->bn == 256;
+  // CTA pairs (256 x 256 tiles, cta_group::2): a pair tile takes ~0.9 of a 128 x 256 tile's time for twice
+  // the rows (measured at 4096^2 x 8192: P 0.81 -> 0.89 of the cuBLAS burst, I 0.69 -> 0.81, W 0.75 ->
+  // 0.84; each SM reads half the B operand from shared memory), over cap/2 pairs; so the estimate is
+  // ceil(pair tiles / (cap / 2)) x 0.9 x (256 + 416).  Rows beyond M in a pair's second half are padding
+  // (M = 384: single CTAs win).  Weight updates that split the batch stay on single CTAs.
+  const long long tp = ((a.Mg + 255) / 256) * ((a.Ng + 255) / 256) * a.groups;
+  const long long cost_pair = ((tp + cap / 2 - 1) / (cap / 2)) * (256 + 416) * 9 / 10;
+  bool pair = a.Ng >= 256 && !splitk && cap >= 2 && cost_pair < (cost256 < cost128 ? cost256 : cost128);
+  if (tune != nullptr && tune->pair == 1) pair = false;
+  if (tune != nullptr && tune->pair == 2) pair = a.Ng >= 256 && !splitk;
+  if (tune != nullptr && tune->bn == 128) pair = false;
+  if (pair)
+    return dtype == IPC_DT_F16 ? dispatch_mode<__half, 256, 1>(a, mode, act, dtype, s, ws, ws_bytes, tune)
+                               : dispatch_mode<__nv_bfloat16, 256, 1>(a, mode, act, dtype, s, ws, ws_bytes, tune);
   if (dtype == IPC_DT_F16)
-    return wide ? dispatch_mode<__half, 256>(a, mode, act, dtype, s, ws, ws_bytes, tune)
-                : dispatch_mode<__half, 128>(a, mode, act, dtype, s, ws, ws_bytes, tune);
-  return wide ? dispatch_mode<__nv_bfloat16, 256>(a, mode, act, dtype, s, ws, ws_bytes, tune)
-              : dispatch_mode<__nv_bfloat16, 128>(a, mode, act, dtype, s, ws, ws_bytes, tune);
+    return wide ? dispatch_mode<__half, 256, 0>(a, mode, act, dtype, s, ws, ws_bytes, tune)
+                : dispatch_mode<__half, 128, 0>(a, mode, act, dtype, s, ws, ws_bytes, tune);
+  return wide ? dispatch_mode<__nv_bfloat16, 256, 0>(a, mode, act, dtype, s, ws, ws_bytes, tune)
+              : dispatch_mode<__nv_bfloat16, 128, 0>(a, mode, act, dtype, s, ws, ws_bytes, tune);
 }
 
 int set_max_ctas(int max_ctas) {

@@ -15,6 +15,7 @@ struct TcTune {
   int splits;    // weight modes: 1 = no split-K, >= 2 = that many batch ranges (bounded by the workspace)
   int raster;    // M-tiles per raster band of the persistent tile walk
   int max_ctas;  // persistent CTAs (further bounded by ipc_set_max_ctas and the SM count)
+  int pair;      // 2: CTA pairs (cta_group::2, 256 x 256 tiles); 0 / 1: single CTAs
 };
 // ws / ws_bytes: optional fp32 workspace for split-K partial tiles (weight modes).
 int launch_tc(const GemmArgs& p, int mode, int act, int dtype, cudaStream_t s, float* ws = nullptr,

@@ -57,14 +57,16 @@ class KernelConfig:
     tc_splits: int = 0
     tc_raster: int = 0
     tc_max_ctas: int = 0
+    tc_pair: int = 0  # CTA pairs (cta_group::2, 256 x 256 tiles): 0 launcher's choice, 1 single CTAs, 2 pairs
 
     def tune(self):
         """The ``ipc_gemm_tune_t`` of this config, or None when every knob is the heuristic's."""
-        if not (self.tc_bn or self.tc_splits or self.tc_raster or self.tc_max_ctas):
+        if not (self.tc_bn or self.tc_splits or self.tc_raster or self.tc_max_ctas or self.tc_pair):
             return None
         t = N.IpcGemmTune()
         t.bn, t.splits, t.raster, t.max_ctas = int(self.tc_bn), int(self.tc_splits), int(self.tc_raster), \
             int(self.tc_max_ctas)
+        t.pair = int(self.tc_pair)
         return t
 
 

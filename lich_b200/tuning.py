@@ -340,7 +340,9 @@ def gemm_candidates(kind: str, M: int, K: int, B: int) -> list[KernelConfig]:
     for bn in (128, 256):
         for raster in (4, 8, 16, 32):
             for sp in splits:
-                out.append(KernelConfig(backend="tcgen05", tc_bn=bn, tc_raster=raster, tc_splits=sp))
+                out.append(KernelConfig(backend="tcgen05", tc_bn=bn, tc_raster=raster, tc_splits=sp, tc_pair=1))
+    for raster in (4, 8, 16, 32):  # CTA pairs (256 x 256 tiles, no split)
+        out.append(KernelConfig(backend="tcgen05", tc_bn=256, tc_raster=raster, tc_pair=2))
     return out
 
 

@@ -107,7 +107,7 @@ def test_measurement_cache(tmp_path):
 def test_sweep_candidates():
     w = T.gemm_candidates("weight", 1024, 1024, 65536)
     p = T.gemm_candidates("prediction", 4096, 4096, 8192)
-    assert len(w) == 1 + 2 * 4 * 6 and len(p) == 1 + 2 * 4
+    assert len(w) == 1 + 2 * 4 * 6 + 4 and len(p) == 1 + 2 * 4 + 4
     assert all(c.backend == "tcgen05" for c in w + p)
     assert len({c for c in w}) == len(w)
 
