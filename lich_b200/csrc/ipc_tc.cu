@@ -879,7 +879,9 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   p.aux2 = a.aux2; p.gs_aux2 = a.gsAux2;
   p.scale = a.scale; p.accumulate = a.accumulate;
   p.a_out_from_stored = a.a_out_from_stored;
-  p.raster = (tune != nullptr && tune->raster > 0) ? tune->raster : TC_RASTER;
+  // default band: 16 single-CTA row tiles = 8 pair tiles (2048 rows either way), so a wave of CTAs covers
+  // a roughly square block of output tiles and re-reads each operand block about as often as the other
+  p.raster = (tune != nullptr && tune->raster > 0) ? tune->raster : (PAIR ? TC_RASTER / 2 : TC_RASTER);
   p.opt = a.opt;
   // split-K: a weight update with fewer output tiles than half the SMs and a long batch reduction
   const int nk = (a.Kg + TC_BK - 1) / TC_BK;

@@ -127,6 +127,7 @@ class TileLangIPC:
             except (OSError, ValueError):
                 self._policy = None
         self._kcfg_cache: dict = {}
+        self._predict_bufs: dict = {}
         if str(cfg.optimizer).lower() not in N.OPT_KINDS:
             raise ValueError(f"unknown optimizer {cfg.optimizer!r} (sgd or adamw)")
         self._opt_state: list | None = None  # per layer (m, v) fp32, allocated at the first update
@@ -788,15 +789,57 @@ class TileLangIPC:
 
     @torch.no_grad()
     def predict(self, x_input: torch.Tensor) -> torch.Tensor:
-        """``h = W[l] @ f(h)`` for ``l = L-1..0`` (reference ``trainer.py:828-833``)."""
+        """``h = W[l] @ f(h)`` for ``l = L-1..0`` (reference ``trainer.py:828-833``).
+
+        Networks the persistent kernel holds (widths <= 64) predict in one launch: its forward sweep
+        gives x[1..L-1], and its first prediction-error pass against a zero target gives
+        ``e[0] = -cast(W[0] f(x[1]))`` (negation is exact), on scratch states -- the model's own states
+        and weights are not written.  Other networks run one fused forward operator per layer."""
         h = x_input.contiguous()
         B = int(h.shape[1])
+        if h.shape[0] != self.cfg.dims[-1]:
+            raise ValueError("input features do not match dims[-1]")
+        if h.dtype == self.cfg.dtype and self._predict_net_ok(B):
+            return self._predict_net(h)
         for l in reversed(range(self.L)):
             out = torch.empty((self.cfg.dims[l], B), device=self.device, dtype=self.cfg.dtype)
             build_forward(self.cfg.dims[l], self.cfg.dims[l + 1], B, self.cfg.activation, self.dtype_name,
                           self._kernel_config("forward", self.cfg.dims[l], self.cfg.dims[l + 1], B))(h, self.w[l], out)
             h = out
         return h
+
+    def _predict_net_ok(self, B: int) -> bool:
+        if not (self.cfg.use_net_kernel and self.cfg.dtype in (torch.float16, torch.bfloat16)
+                and 1 <= self.L <= N.NET_MAX_LAYERS):
+            return False
+        plan = N.net_plan(self.cfg.dims, int(B), 1, int(self.cfg.net_cluster))
+        return plan is not None and plan[0] > 0  # the small-width cluster kernel
+
+    def _predict_net(self, x_input: torch.Tensor) -> torch.Tensor:
+        B = int(x_input.shape[1])
+        d, dt = self.cfg.dims, self.cfg.dtype
+        bufs = self._predict_bufs.get(B)
+        if bufs is None:  # scratch states of the prediction launch, per batch size
+            xs = [torch.zeros((dv, B), device=self.device, dtype=dt) for dv in d]
+            es = [torch.zeros((dv, B), device=self.device, dtype=dt) for dv in d]
+            bufs = self._predict_bufs[B] = (xs, es)
+        xs, es = bufs
+        xs[0].zero_()
+        xs[-1].copy_(x_input)
+        desc = N.IpcNet()
+        desc.L, desc.B, desc.nets = self.L, B, 1
+        for l, dv in enumerate(d):
+            desc.dims[l] = int(dv)
+            desc.x[l] = xs[l].data_ptr()
+        for l in range(self.L):
+            desc.w[l] = self.w[l].data_ptr()
+            desc.e[l] = es[l].data_ptr()
+        run = N.IpcNetRun()
+        run.steps, run.T, run.forward_init, run.update_weights, run.recompute = 1, 1, 1, 0, 1
+        run.alpha, run.gamma = float(self.cfg.alpha), float(self.cfg.gamma)
+        run.act, run.dtype, run.cluster = self.act.code, N.dtype_code(dt), int(self.cfg.net_cluster)
+        N.check(N.load().ipc_net_train(desc, run, N.stream_handle(self.device)))
+        return -es[0]
 
     @torch.no_grad()
     def evaluate(self, x_input: torch.Tensor, labels: torch.Tensor, *,

@@ -215,3 +215,30 @@ def test_evaluate_counts_argmax_on_device(dims, dtype):
     N.check(N.load().ipc_count_correct(tie.data_ptr(), 4, 8, lab.data_ptr(), c.data_ptr(), N.dtype_code(torch.float16),
                                        N.stream_handle(DEV)))
     assert int(c.item()) == 8
+
+
+@pytest.mark.parametrize("depth,B", [(3, 128), (6, 96), (4, 8)])
+def test_predict_single_launch_matches_layer_chain(depth, B):
+    """Hidden-64 networks predict in one persistent-kernel launch (forward sweep + a prediction-error pass
+    against a zero target); the answer matches the per-layer forward operators (both storage-round each
+    layer) and the fp32 oracle's forward chain, and the model's states are untouched."""
+    from lich_b200 import _native as N
+    from lich_b200 import synthetic as S
+    from lich_b200.trainer import TileLangIPC
+    dims = S.paper_dims(depth)
+    m = TileLangIPC(_cfg(dims, torch.float16), device=DEV, seed=21)
+    (x, y), = S.batch_pool(784, 10, B, count=1, seed=22)
+    xd = x.to(DEV, torch.float16)
+    m.train_step(xd, y.to(DEV, torch.float16), T=2)
+    state = [t.clone() for t in m.x + m.e[:-1]]
+    n0 = N.launch_count()
+    fused = m.predict(xd)
+    assert N.launch_count() - n0 == 1
+    assert all(torch.equal(a, b) for a, b in zip(state, m.x + m.e[:-1]))
+    m.cfg = type(m.cfg)(**{**m.cfg.__dict__, "use_net_kernel": False})
+    chain = m.predict(xd)
+    assert O.rel_inf(fused.cpu(), chain.cpu()) <= 1e-2
+    h = x.to(torch.float16).float()
+    for l in reversed(range(len(dims) - 1)):
+        h = m.w[l].float().cpu() @ torch.tanh(h)
+    assert O.rel_inf(fused.cpu(), h) <= 2e-2
