@@ -85,6 +85,7 @@ class ClockSampler:
         self._thread = None
         self._stop = None
         self._nvml = None
+        self._handle = None
 
     def _nvml_handle(self):
         import pynvml
@@ -95,15 +96,18 @@ class ClockSampler:
         except Exception:
             return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
+    def _take(self, nv, h):
+        try:
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            self.rows.append((float(sm), float(mx), int(bits)))
+        except Exception:
+            pass
+
     def _poll(self, nv, h):
         while not self._stop.is_set():
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
-                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                self.rows.append((float(sm), float(mx), int(bits)))
-            except Exception:
-                pass
+            self._take(nv, h)
             self._stop.wait(self.period)
 
     def __enter__(self):
@@ -112,6 +116,7 @@ class ClockSampler:
             nv, h = self._nvml_handle()
             self._nvml = nv
             self._stop = threading.Event()
+            self._handle = h
             self._thread = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
             self._thread.start()
             return self
@@ -130,6 +135,7 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self._thread is not None:
+            self._take(self._nvml, self._handle)  # the clock as the timed region ends
             self._stop.set()
             self._thread.join(timeout=5)
         if self.proc is not None:
@@ -150,8 +156,12 @@ class ClockSampler:
             os.unlink(self.path)
 
     def mark(self):
-        """Drop the samples taken so far (the warm-up that ran inside the sampler's window)."""
+        """Drop the samples taken so far (the warm-up that ran inside the sampler's window) and take one
+        as the timed region starts, so a region shorter than the polling period still has the samples
+        at its two ends."""
         self.rows = []
+        if self._thread is not None:
+            self._take(self._nvml, self._handle)
 
     def summary(self):
         if self._thread is None and self.proc is None:
@@ -454,6 +464,8 @@ def run_c5(args, world, rank, local):
     dp_kw = {"reduce": args.dp_reduce}
     if args.comm_sms >= 0:
         dp_kw["comm_sms"] = args.comm_sms
+    if args.comm_sms_min >= 0:
+        dp_kw["comm_sms_min"] = args.comm_sms_min
     dp = DataParallelIPC(cfg, device=dev, **dp_kw)
     w_init = [w.to(dev, dtype) for w in S.fan_in_normal(dims, seed=1)]
     g = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -549,6 +561,7 @@ def run_c5(args, world, rank, local):
         "config": {"workload": C5_WORKLOAD,
                    "global_batch": Bg, "batch_per_rank": B, "T": T, "parallelism": f"dp{world}",
                    "comm_sms": dp.comm_sms if world > 1 else 0,
+                   "comm_sms_min": dp.comm_sms_min if world > 1 else 0,
                    "dp_reduce": dp.reduce if world > 1 else None,
                    "step_breakdown_ms": breakdown,
                    "l2": "inputs larger than L2 (the per-step state is GBs)"},
@@ -1140,6 +1153,8 @@ def main():
     ap.add_argument("--chunk", type=int, default=500, help="training steps per persistent-kernel launch")
     ap.add_argument("--comm-sms", type=int, default=-1,
                     help="c5: SMs the delta GEMMs leave to the overlapped all-reduces (default: DataParallelIPC's)")
+    ap.add_argument("--comm-sms-min", type=int, default=-1,
+                    help="c5: fewest SMs a delta GEMM may leave when more CTAs save it a wave of tiles")
     ap.add_argument("--dp-reduce", choices=["rs_ag", "allreduce"], default="rs_ag",
                     help="c5: reduce-scatter + sliced apply + all-gather, or one all-reduce per layer")
     ap.add_argument("--no-cpu-baseline", action="store_true")

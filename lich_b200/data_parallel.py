@@ -16,7 +16,9 @@ replicas identical.  While reductions are in flight the persistent GEMMs
 leave ``comm_sms`` SMs free (``ipc_set_max_ctas``): with every SM taken by a
 GEMM CTA, the collective's kernels would wait for the GEMM and the overlap
 would be lost.  Each layer's sum is applied as soon as its own reduction is
-done.
+done: layer l's apply is queued behind the next layer's delta GEMM, which its
+reduction runs beside, so only the last layer's reduction and apply follow the
+last GEMM.
 
 ``reduce="rs_ag"`` (the default when a layer's size divides by the world)
 splits the all-reduce into its halves around the apply: a reduce-scatter of
@@ -54,15 +56,23 @@ class DataParallelIPC:
     """Replicated weights, batch shards, one fp32 dW reduction per layer per training step."""
 
     def __init__(self, cfg: IPCConfig, *, device: torch.device, group=None, seed: int = 0,
-                 model: TileLangIPC | None = None, comm_sms: int = 24, reduce: str = "rs_ag"):
+                 model: TileLangIPC | None = None, comm_sms: int = 24, comm_sms_min: int | None = None,
+                 reduce: str = "rs_ag"):
         """comm_sms: SMs the delta GEMMs leave to the reductions they overlap (world > 1).
+        comm_sms_min: if below comm_sms, a delta GEMM may leave as few as this many SMs when the extra
+        CTAs save it a wave of output tiles (e.g. 4096 x 4096 = 256 tiles of 256 x 256: 5 waves on 62
+        CTA pairs, 4 on 64).
         reduce: "rs_ag" (reduce-scatter, sliced apply, all-gather) or "allreduce"."""
         if comm_sms < 0:
             raise ValueError("comm_sms must be >= 0")
+        comm_sms_min = comm_sms if comm_sms_min is None else int(comm_sms_min)
+        if not 0 <= comm_sms_min <= comm_sms:
+            raise ValueError("comm_sms_min must be in [0, comm_sms]")
         if reduce not in ("rs_ag", "allreduce"):
             raise ValueError(f"unknown reduce {reduce!r}")
         self.group = group
         self.comm_sms = int(comm_sms)
+        self.comm_sms_min = comm_sms_min
         self.reduce = reduce
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
@@ -99,13 +109,31 @@ class DataParallelIPC:
             N.fused_gemm(N.MODE_WDELTA, m.e[l], m.x[l + 1], dw, M=d[l], K=d[l + 1], B=B, scale=self.cfg.alpha,
                          flags=N.FLAG_ACTIVATE_B, act=self.cfg.activation, dtype=self.cfg.dtype, device=m.device)
 
+    def _sms(self) -> int:
+        return torch.cuda.get_device_properties(self.model.w[0].device).multi_processor_count
+
+    def _leave_for(self, l: int) -> int:
+        """SMs the delta GEMM of layer l leaves to the reductions in flight: comm_sms, or fewer (down to
+        comm_sms_min) where the CTAs gained finish the layer's 256 x 256 output tiles in fewer waves (the
+        persistent GEMM takes ceil(tiles / CTA pairs) tile times); the most SMs among the fewest waves."""
+        if self.comm_sms_min >= self.comm_sms:
+            return self.comm_sms
+        d = self.cfg.dims
+        tiles = -(-d[l] // 256) * -(-d[l + 1] // 256)
+        sms = self._sms()
+        best = None
+        for leave in range(self.comm_sms, self.comm_sms_min - 1, -1):
+            waves = -(-tiles // max(1, (sms - leave) // 2))
+            if best is None or waves < best[0]:
+                best = (waves, leave)
+        return best[1]
+
     def _cap(self, leave: int) -> None:
         """Leave `leave` SMs free of persistent GEMM CTAs (0 lifts the cap)."""
         if leave <= 0:
             N.set_max_ctas(0)
             return
-        sms = torch.cuda.get_device_properties(self.model.w[0].device).multi_processor_count
-        N.set_max_ctas(max(1, sms - leave))
+        N.set_max_ctas(max(1, self._sms() - leave))
 
     def _apply(self, l: int, dw: torch.Tensor) -> None:
         w = self.model.w[l]
@@ -158,10 +186,25 @@ class DataParallelIPC:
         mark("inference")
         L = len(self.cfg.dims) - 1
         order = sorted(range(L), key=lambda l: -self._dw[l].numel())  # biggest reductions start first
-        handles = {}
+        handles, gathers, pending = {}, [], []
+
+        def finish(l):
+            # the stream waits for layer l's reduction, applies it and (sliced) starts its all-gather
+            if l in handles:
+                handles.pop(l).wait()
+            if self._sliced(l):
+                n = self._dw[l].numel() // self.world
+                lo, hi = self.rank * n, (self.rank + 1) * n
+                self._apply_slice(l, lo, hi)
+                gathers.append(self._all_gather(l, lo, hi))
+            else:
+                self._apply(l, self._dw[l])
+
         capped = False
         try:
             for l in order:
+                if capped:
+                    self._cap(self._leave_for(l))
                 self._delta(l, self._dw[l])
                 if self._sliced(l):
                     n = self._dw[l].numel() // self.world
@@ -170,24 +213,19 @@ class DataParallelIPC:
                     hs = allreduce_deltas([self._dw[l]], self.group, async_op=True)
                     if hs:
                         handles[l] = hs[0]
+                # the previous layer's reduction ran beside this layer's GEMM: apply it now, so its
+                # all-gather overlaps the next GEMM instead of queueing behind the last one
+                if pending:
+                    finish(pending.pop(0))
+                pending.append(l)
                 if l in handles and not capped and self.comm_sms > 0:
-                    self._cap(self.comm_sms)
                     capped = True
         finally:
             if capped:
                 self._cap(0)
         mark("deltas")
-        gathers = []
-        for l in order:
-            if l in handles:
-                handles[l].wait()
-            if self._sliced(l):
-                n = self._dw[l].numel() // self.world
-                lo, hi = self.rank * n, (self.rank + 1) * n
-                self._apply_slice(l, lo, hi)
-                gathers.append(self._all_gather(l, lo, hi))
-            else:
-                self._apply(l, self._dw[l])
+        for l in pending:
+            finish(l)
         for h in gathers:
             h.wait()
         mark("end")

@@ -108,10 +108,13 @@ def test_sharded_step_equals_full_batch_step(reduce):
     x_ref, w_ref, _, _ = O.train_step(x, y, w0, act=ACT, alpha=ALPHA, gamma=GAMMA, T=T)
     for rank in range(2):
         w_got, x_got, caps = res[rank]
-        # the delta GEMMs after the first all-reduce leave SMs to it; the cap is lifted before the
-        # applies, and every layer is applied once
-        assert caps[0] == ("cap", 24) and caps[1] == ("cap", 0), caps
-        assert sorted(l for k, l in caps[2:] if k == "apply") == list(range(len(w0))), caps
+        # the delta GEMMs after the first reduction leave SMs to it; each layer is applied once, behind
+        # the next layer's delta GEMM, and only the last layer's apply follows the lifted cap
+        assert caps[0] == ("cap", 24), caps
+        lift = caps.index(("cap", 0))
+        assert [k for k, _ in caps[lift + 1:]] == ["apply"] and caps[lift - 1][0] == "apply", caps
+        assert all(c == ("cap", 24) for c in caps[:lift] if c[0] == "cap"), caps
+        assert sorted(l for k, l in caps if k == "apply") == list(range(len(w0))), caps
         for l in range(len(w_ref)):
             assert O.rel_inf(w_got[l], w_ref[l]) <= 1e-5, (rank, "w", l)
         cols = slice(rank * B // 2, (rank + 1) * B // 2)
@@ -125,3 +128,21 @@ def test_single_process_allreduce_is_identity():
     from lich_b200.data_parallel import allreduce_deltas
     d = [torch.ones(3)]
     assert allreduce_deltas(d) == [] and torch.equal(d[0], torch.ones(3))
+
+
+def test_delta_cap_saves_waves():
+    """comm_sms_min < comm_sms: a delta GEMM takes the extra CTAs only where they save a wave of
+    256 x 256 output tiles (148 SMs: 4096^2 = 256 tiles, 5 waves on 62 pairs, 4 on 64)."""
+    from lich_b200.data_parallel import DataParallelIPC
+
+    m = _OracleModel([torch.zeros(a, b) for a, b in zip(DIMS[:-1], DIMS[1:])])
+    m.cfg = _Cfg(dims=(1000, 4096, 4096, 300))
+    dp = DataParallelIPC(m.cfg, device=torch.device("cpu"), model=m, comm_sms=24, comm_sms_min=16)
+    dp._sms = lambda: 148
+    assert dp._leave_for(1) == 20          # 256 tiles: 64 pairs -> 4 waves
+    assert dp._leave_for(0) == 20          # 4 x 16 = 64 tiles: one wave on 64 pairs
+    assert dp._leave_for(2) == 24          # 16 x 2 = 32 tiles: one wave already
+    fixed = DataParallelIPC(m.cfg, device=torch.device("cpu"), model=m, comm_sms=24)
+    assert fixed._leave_for(1) == 24
+    with pytest.raises(ValueError):
+        DataParallelIPC(m.cfg, device=torch.device("cpu"), model=m, comm_sms=24, comm_sms_min=30)
