@@ -197,7 +197,24 @@ def torch_dtype(dtype) -> torch.dtype:
 
 
 def net_plan(dims, B: int, nets: int = 1, cluster: int = 0) -> tuple[int, int] | None:
-    """(cluster, shared-memory bytes) the persistent kernel would use, or None if it cannot run."""
+    """(cluster, shared-memory bytes) the persistent kernel would use, or None if it cannot run.
+
+    A pure function of its arguments on a given device kind: remembered per process (the trainer asks
+    before every launch)."""
+    key = (tuple(int(d) for d in dims), int(B), int(nets), int(cluster))
+    hit = _NET_PLANS.get(key, _MISS)
+    if hit is not _MISS:
+        return hit
+    res = _net_plan(key[0], *key[1:])
+    _NET_PLANS[key] = res
+    return res
+
+
+_NET_PLANS: dict = {}
+_MISS = object()
+
+
+def _net_plan(dims, B: int, nets: int, cluster: int) -> tuple[int, int] | None:
     desc = IpcNet()
     desc.L = len(dims) - 1
     if not 1 <= desc.L <= NET_MAX_LAYERS:

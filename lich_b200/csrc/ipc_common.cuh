@@ -183,4 +183,26 @@ int require_sm100();
 
 inline size_t dt_size(int dtype) { return dtype == IPC_DT_F32 ? 4 : 2; }
 
+// cudaFuncSetAttribute for a kernel's dynamic shared memory (and, with non_portable, the opt-in to
+// clusters of more than 8 CTAs) once per kernel, device and size instead of on every launch: the
+// attributes last as long as the device's context, and setting them costs microseconds of host time
+// in front of launches that are themselves tens of microseconds long.  The record is per process; a
+// context destroyed by cudaDeviceReset loses the attributes, and the next launch that needs them
+// fails with a launch error.
+template <auto KERN>
+cudaError_t ensure_kernel_smem(int bytes, bool non_portable = false) {
+  static int done[64][2] = {};  // per device: dynamic bytes set, non-portable set (benign races)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = -1;
+  if (dev >= 0 && done[dev][0] >= bytes && (!non_portable || done[dev][1])) return cudaSuccess;
+  cudaError_t err = cudaFuncSetAttribute(KERN, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess && non_portable)
+    err = cudaFuncSetAttribute(KERN, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (err == cudaSuccess && dev >= 0) {
+    if (done[dev][0] < bytes) done[dev][0] = bytes;
+    if (non_portable) done[dev][1] = 1;
+  }
+  return err;
+}
+
 }  // namespace ipc

@@ -968,9 +968,7 @@ int choose_plan(NetParams<T>& p, int want, int* ncol_out) {
 template <typename T, int ACT, int NCOL>
 int launch_net_t(NetParams<T>& p, cudaStream_t s) {
   auto kern = net_kernel_act<T, ACT, NCOL>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem_bytes);
-  if (err == cudaSuccess && p.C > MAX_PORTABLE_CLUSTER)
-    err = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t err = ensure_kernel_smem<net_kernel_act<T, ACT, NCOL>>(p.smem_bytes, p.C > MAX_PORTABLE_CLUSTER);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "net kernel smem attribute: %s", cudaGetErrorString(err));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.C, p.nets, 1);

@@ -204,7 +204,7 @@ int launch_skinny_t(const GemmArgs& p, cudaStream_t s) {
   if (mtiles > 65535 || p.groups > 65535)
     return set_error(IPC_ERR_ARG, "small-batch GEMM grid too large (M=%d groups=%d)", p.Mg, p.groups);
   auto kern = skinny_kernel<T, ACT, MODE, BACT, NB>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t err = ensure_kernel_smem<skinny_kernel<T, ACT, MODE, BACT, NB>>((int)smem);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "small-batch GEMM smem attribute: %s", cudaGetErrorString(err));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(C, mtiles, p.groups);

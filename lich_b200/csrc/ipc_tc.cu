@@ -333,6 +333,26 @@ __device__ __forceinline__ uint4 epi_vec_pw(uint4 in, const uint32_t* acc8, floa
   return o;
 }
 
+// F through the transpose buffer: a row thread packs 8 accumulators into cast(acc) ...
+template <typename T>
+__device__ __forceinline__ uint4 pack_vec(const uint32_t* acc8) {
+  uint4 o;
+  T* oh = reinterpret_cast<T*>(&o);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) oh[j] = St<T>::st(__uint_as_float(acc8[j]));
+  return o;
+}
+// ... and the coalesced pass stores it and cast(f(x)) of the stored x (the A_out of the forward sweep)
+template <typename T, int ACT>
+__device__ __forceinline__ uint4 act_vec(uint4 x) {
+  const T* h = reinterpret_cast<const T*>(&x);
+  uint4 o;
+  T* oh = reinterpret_cast<T*>(&o);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) oh[j] = St<T>::st(act_f_hw<ACT>(St<T>::ld(h[j])));
+  return o;
+}
+
 template <typename T, int ACT>
 __device__ __forceinline__ void epi_vec_i(uint4 ev, uint4& xv, uint4& av, const uint32_t* acc8, float gamma,
                                           int from_stored) {
@@ -379,7 +399,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr bool EPI_STAGED = (MODE == MODE_P || MODE == MODE_W || MODE == MODE_I);
+  constexpr bool EPI_STAGED =
+      (MODE == MODE_P || MODE == MODE_W || MODE == MODE_I || MODE == MODE_F || MODE == MODE_WD);
   constexpr uint32_t EPI_REGION = EPI_STAGED ? EPI_BYTES : 0;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + EPI_REGION);
   // bars: full[S], empty[S], tfull[2], tempty[2], epilogue slots[2 per epilogue warp]
@@ -549,7 +570,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint32_t aphase = 0;
     bool staged = false;
     if constexpr (EPI_STAGED) staged = p.staged != 0;
-    const bool xpose = (MODE == MODE_P || MODE == MODE_W) && staged;
+    const bool xpose = (MODE == MODE_P || MODE == MODE_W || MODE == MODE_F) && staged;
     if (xpose) {
       {
         // P / W: the warp's 32 x HC block of the in/out operand (X_lo or W) is read with coalesced
@@ -557,6 +578,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // this one is in shared memory), then per 64-column chunk: registers -> swizzled shared
         // buffer, each row thread applies the epilogue to its row in place, and the chunk leaves
         // with coalesced 16-byte stores (a warp instruction covers 4 rows x 128 bytes).
+        // F has no input block: the row threads write cast(acc) into the buffer, and the coalesced
+        // pass stores it and, when A_out is given, cast(f(x)) beside it.
+        constexpr bool HAS_IN = (MODE != MODE_F);
         constexpr int NCH = HC / 64;        // 64-column chunks per warp and tile
         constexpr int NPRE = 8 * NCH;       // prefetched 16-byte vectors per thread
         const uint32_t xb = saddr(smem + STAGES * STAGE_BYTES) + (warp - 2) * EPI_WARP_BYTES;
@@ -579,7 +603,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
           }
         };
-        if (unit0 < p.tiles) prefetch(unit0);
+        if (HAS_IN && unit0 < p.tiles) prefetch(unit0);
         for (int t = unit0; t < p.tiles; t += units) {
           int g, m0, n0, sp;
           tile_coords(p, t, BN, g, m0, n0, sp, TM, rank);
@@ -591,13 +615,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const uint32_t trow = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
 #pragma unroll
           for (int cc = 0; cc < NCH; ++cc) {
-            // registers -> shared (row 4i + cr, vector cj; 128-byte rows, vector index ^ (row & 7))
+            if constexpr (HAS_IN) {
+              // registers -> shared (row 4i + cr, vector cj; 128-byte rows, vector index ^ (row & 7))
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int r = 4 * i + cr;
-              sts128(xb + r * 128 + ((cj ^ (r & 7)) << 4), pre[8 * cc + i]);
+              for (int i = 0; i < 8; ++i) {
+                const int r = 4 * i + cr;
+                sts128(xb + r * 128 + ((cj ^ (r & 7)) << 4), pre[8 * cc + i]);
+              }
+              if (cc == NCH - 1 && t + units < p.tiles) prefetch(t + units);
             }
-            if (cc == NCH - 1 && t + units < p.tiles) prefetch(t + units);
             __syncwarp();
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
@@ -606,7 +632,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const uint32_t a = xb + lane * 128 + (((4 * hf + j) ^ (lane & 7)) << 4);
-                sts128(a, epi_vec_pw<T, MODE>(lds128(a), raw + 8 * j, p.scale));
+                if constexpr (HAS_IN)
+                  sts128(a, epi_vec_pw<T, MODE>(lds128(a), raw + 8 * j, p.scale));
+                else
+                  sts128(a, pack_vec<T>(raw + 8 * j));
               }
             }
             if (cc == NCH - 1) {  // every accumulator column read: release it to the MMA warp
@@ -618,8 +647,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int i = 0; i < 8; ++i) {
               const int r = 4 * i + cr, n = nw + 64 * cc + 8 * cj;
               const uint4 v = lds128(xb + r * 128 + ((cj ^ (r & 7)) << 4));
-              if (r0 + r < p.Mg && n < p.Ng)
+              if (r0 + r < p.Mg && n < p.Ng) {
                 *reinterpret_cast<uint4*>(dst + g * p.gs_out + (long long)(r0 + r) * p.ld_out + n) = v;
+                if constexpr (MODE == MODE_F) {
+                  if (p.aux2 != nullptr)
+                    *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.aux2) + g * p.gs_aux2 +
+                                              (long long)(r0 + r) * p.ld_out + n) = act_vec<T, ACT>(v);
+                }
+              }
             }
             __syncwarp();
           }
@@ -712,6 +747,49 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           bulk_wait0();
         }
         __syncwarp();
+      } else if constexpr (MODE == MODE_WD) {
+        // WD (dw = scale * acc in fp32): per 32-column chunk the row threads write their scaled
+        // accumulators into the swizzled buffer (128-byte rows, vector index ^ (row & 7)), and the warp
+        // stores the chunk with coalesced 16-byte stores (an instruction covers 4 rows x 128 bytes)
+        const uint32_t xb = saddr(smem + STAGES * STAGE_BYTES) + (warp - 2) * EPI_WARP_BYTES;
+        float* dst = reinterpret_cast<float*>(p.out);
+        const int cr = lane >> 3, cj = lane & 7;
+        for (int t = unit0; t < p.tiles; t += units) {
+          int g, m0, n0, sp;
+          tile_coords(p, t, BN, g, m0, n0, sp, TM, rank);
+          const int r0 = m0 + 32 * q, nw = n0 + c_lo;
+          const bool ok = mbar_wait(tfull0 + 8 * acc, aphase, abort_flag);
+          __syncwarp();
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t trow = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
+#pragma unroll 1
+          for (int c = 0; c < HC / 32; ++c) {
+            uint32_t raw[32];
+            tmem_ld32(trow + c_lo + 32 * c, raw);
+            if (c == HC / 32 - 1) {  // every accumulator column read: release it to the MMA warp
+              tc_fence_before();
+              release_acc(tempty0 + 8 * acc);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              sts128(xb + lane * 128 + ((j ^ (lane & 7)) << 4),
+                     make_uint4(__float_as_uint(p.scale * __uint_as_float(raw[4 * j])),
+                                __float_as_uint(p.scale * __uint_as_float(raw[4 * j + 1])),
+                                __float_as_uint(p.scale * __uint_as_float(raw[4 * j + 2])),
+                                __float_as_uint(p.scale * __uint_as_float(raw[4 * j + 3]))));
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = 4 * i + cr, n = nw + 32 * c + 4 * cj;
+              const uint4 v = lds128(xb + r * 128 + ((cj ^ (r & 7)) << 4));
+              if (r0 + r < p.Mg && n < p.Ng)
+                *reinterpret_cast<uint4*>(dst + g * p.gs_out + (long long)(r0 + r) * p.ld_out + n) = v;
+            }
+            __syncwarp();
+          }
+          if (++acc == 2) { acc = 0; aphase ^= 1; }
+        }
       }
     } else {
       for (int t = unit0; t < p.tiles; t += units) {
@@ -907,10 +985,12 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   p.tiles *= p.splits;
   // staged epilogue (no split-K): P / W through the transpose buffer, I through TMA with three maps
   // (E, X, A_out) of 32-row x 16-column boxes, 32-byte swizzle
-  constexpr bool EPI_STAGED = (MODE == MODE_P || MODE == MODE_W || MODE == MODE_I);
+  constexpr bool EPI_STAGED =
+      (MODE == MODE_P || MODE == MODE_W || MODE == MODE_I || MODE == MODE_F || MODE == MODE_WD);
   CUtensorMap te[3];
   memset(te, 0, sizeof(te));
-  p.staged = EPI_STAGED && p.splits == 1;
+  // WD accumulating into dw reads dw back per element: the row-per-thread path
+  p.staged = EPI_STAGED && p.splits == 1 && !(MODE == MODE_WD && a.accumulate);
   if (MODE == MODE_I && p.staged) {
     const void* src[3] = {a.aux, a.out, a.aux2};
     const long long gs[3] = {a.gsAux, a.gsOut, a.gsAux2};
@@ -926,7 +1006,7 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   constexpr int TAIL = ((2 * STAGES + 4 + 2 * TC_EPI_WARPS) * 8 + 8 + 255) / 256 * 256;
   const int smem = STAGES * STAGE_BYTES + (EPI_STAGED ? EPI_BYTES : 0) + 1024 + TAIL;
   auto kern = tc_gemm_kernel<T, ACT, MODE, BN, PAIR>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t err = ensure_kernel_smem<tc_gemm_kernel<T, ACT, MODE, BN, PAIR>>(smem);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "tcgen05 kernel smem attribute: %s", cudaGetErrorString(err));
   if constexpr (PAIR) {
     // clusters of two CTAs, one pair per two SMs, each pair walking 256-row tiles

@@ -553,12 +553,19 @@ int wn_prepare(WideParams<T>& p, const ipc_net_t* net, const ipc_net_run_t* run,
 template <typename T, int ACT, bool PAIRS, bool ACC>
 int wn_launch(const WideParams<T>& p, size_t smem, cudaStream_t s) {
   auto kern = wide_net_kernel<T, ACT, PAIRS, ACC>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t err = ensure_kernel_smem<wide_net_kernel<T, ACT, PAIRS, ACC>>((int)smem);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "wide net kernel smem attribute: %s", cudaGetErrorString(err));
   int dev = 0, sms = 0, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WN_THREADS, smem);
+  // residency check once per device and size (the answer does not change within a process)
+  static long long checked[64] = {};  // smem bytes + 1 of the last successful check
+  if (dev >= 0 && dev < 64 && checked[dev] == (long long)smem + 1) {
+    per_sm = 1;
+  } else {
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WN_THREADS, smem);
+    if (err == cudaSuccess && per_sm >= 1 && dev >= 0 && dev < 64) checked[dev] = (long long)smem + 1;
+  }
   if (err != cudaSuccess || per_sm < 1)
     return set_error(IPC_ERR_UNSUPPORTED, "wide net kernel: no resident CTA per SM (%s)", cudaGetErrorString(err));
   cudaLaunchConfig_t cfg = {};

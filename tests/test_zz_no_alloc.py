@@ -8,6 +8,8 @@ call, calls change the device's free memory by nothing.  Requests beyond the
 scratch limit, and modes other than the weight update, return IPC_ERR_ARG.
 The file is named to be collected last; it also passes alone.
 """
+import gc
+
 import pytest
 import torch
 
@@ -55,17 +57,23 @@ def test_noalloc_matches_existing_entry_point_twice(case, dt):
         outs = []
         for call in range(2):
             out = fresh()
-            torch.cuda.synchronize()
-            free0 = torch.cuda.mem_get_info(DEV)[0]
-            alloc0 = torch.cuda.memory_allocated(DEV)
-            n0 = N.launch_count()
-            rc = _noalloc(mode, e, a, out, G, M, K, B, alpha, dt)
-            assert rc == N.IPC_OK, N.load().ipc_last_error().decode()
-            torch.cuda.synchronize()
-            assert N.launch_count() - n0 == 2  # the split GEMM and its reduce pass, nothing else
-            assert torch.cuda.memory_allocated(DEV) == alloc0  # nothing through torch's allocator
-            if call == 1:  # the first call may load the scratch; later calls allocate nothing
-                assert torch.cuda.mem_get_info(DEV)[0] == free0
+            # garbage of earlier tests collected inside the measured window would free memory there
+            gc.collect()
+            gc.disable()
+            try:
+                torch.cuda.synchronize()
+                free0 = torch.cuda.mem_get_info(DEV)[0]
+                alloc0 = torch.cuda.memory_allocated(DEV)
+                n0 = N.launch_count()
+                rc = _noalloc(mode, e, a, out, G, M, K, B, alpha, dt)
+                assert rc == N.IPC_OK, N.load().ipc_last_error().decode()
+                torch.cuda.synchronize()
+                assert N.launch_count() - n0 == 2  # the split GEMM and its reduce pass, nothing else
+                assert torch.cuda.memory_allocated(DEV) == alloc0  # nothing through torch's allocator
+                if call == 1:  # the first call may load the scratch; later calls allocate nothing
+                    assert torch.cuda.mem_get_info(DEV)[0] == free0
+            finally:
+                gc.enable()
             outs.append(out)
         assert N.device_status() == 0
         for out in outs:
