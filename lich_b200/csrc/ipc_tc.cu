@@ -63,12 +63,19 @@ constexpr int TC_EPI_WARPS = 8;                     // two per TMEM lane quarter
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;  // TMA warp + MMA warp + epilogue
 constexpr long long TC_WAIT_NS = 2000000000LL;
 
-// Epilogue staging through shared memory (P, W, I without split-K): 4 KB per epilogue warp.  P / W
-// use it as one 32-row x 64-column transpose buffer (128-byte rows); I as two 2 KB slots, each holding
-// an E tile and an X tile of 32 rows x 16 columns (32-byte rows, TMA 32-byte swizzle).
+// Epilogue staging through shared memory (P, W, F, WD, I without split-K).  P / W / F / WD use 4 KB
+// per epilogue warp as one 32-row x 128-byte transpose buffer; I uses 2 KB slots, each holding an E
+// tile and an X tile of 32 rows x 16 columns (32-byte rows, TMA 32-byte swizzle): two per warp, or
+// four in the CTA-pair form, which gives the mainloop one stage less (5 x 32 KB) so that an I epilogue
+// keeps three chunks' loads in flight -- the epilogue streams four operands (E, X in; X, A_out out)
+// and bounds the kernel when the reduction is short (K = 1000: a tile's MMAs take ~7 us).
 constexpr int EPI_SLOT = 2048;
-constexpr int EPI_WARP_BYTES = 2 * EPI_SLOT;
-constexpr int EPI_BYTES = TC_EPI_WARPS * EPI_WARP_BYTES;
+__host__ __device__ constexpr int epi_slots(int mode, int pair) { return (mode == MODE_I && pair) ? 4 : 2; }
+__host__ __device__ constexpr int epi_warp_bytes(int mode, int pair) { return epi_slots(mode, pair) * EPI_SLOT; }
+__host__ __device__ constexpr int epi_bytes(int mode, int pair) { return TC_EPI_WARPS * epi_warp_bytes(mode, pair); }
+__host__ __device__ constexpr int tc_stages(int mode, int pair) {
+  return pair ? (mode == MODE_I ? TC_STAGES_PAIR - 1 : TC_STAGES_PAIR) : TC_STAGES;
+}
 
 constexpr int TC_RASTER = 16;  // default M-tiles per raster band: a wave covers ~16 x 9 tiles, both operands in L2
 
@@ -387,7 +394,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   constexpr int NCTA = PAIR ? 2 : 1;
   constexpr int TM = TC_BM * NCTA;    // rows of a tile
   constexpr int BNL = BN / NCTA;      // columns of B this CTA loads
-  constexpr int STAGES = PAIR ? TC_STAGES_PAIR : TC_STAGES;
+  constexpr int STAGES = tc_stages(MODE, PAIR);
+  constexpr int NSL = epi_slots(MODE, PAIR);             // I epilogue slots per warp
+  constexpr int EPI_WARP_BYTES = epi_warp_bytes(MODE, PAIR);
   constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
   constexpr uint32_t B_BYTES = BNL * TC_BK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -401,10 +410,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr bool EPI_STAGED =
       (MODE == MODE_P || MODE == MODE_W || MODE == MODE_I || MODE == MODE_F || MODE == MODE_WD);
-  constexpr uint32_t EPI_REGION = EPI_STAGED ? EPI_BYTES : 0;
+  constexpr uint32_t EPI_REGION = EPI_STAGED ? epi_bytes(MODE, PAIR) : 0;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + EPI_REGION);
-  // bars: full[S], empty[S], tfull[2], tempty[2], epilogue slots[2 per epilogue warp]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4 + 2 * TC_EPI_WARPS);
+  // bars: full[S], empty[S], tfull[2], tempty[2], epilogue slots[NSL per epilogue warp]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4 + NSL * TC_EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const uint32_t full0 = saddr(bars), empty0 = saddr(bars + STAGES);
   const uint32_t tfull0 = saddr(bars + 2 * STAGES), tempty0 = saddr(bars + 2 * STAGES + 2);
@@ -424,7 +433,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(tfull0 + 8 * b, 1);
       mbar_init(tempty0 + 8 * b, 32 * TC_EPI_WARPS * NCTA);
     }
-    for (int b = 0; b < 2 * TC_EPI_WARPS; ++b) mbar_init(ebar0 + 8 * b, 1);
+    for (int b = 0; b < NSL * TC_EPI_WARPS; ++b) mbar_init(ebar0 + 8 * b, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -663,14 +672,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     } else if (staged) {
       if constexpr (MODE == MODE_I) {
-        // I: E and X staged through shared memory in 16-column chunks (two 2 KB slots per warp).
-        // The first two chunks are requested with TMA before the accumulator is ready; chunk s + 2 as
-        // soon as chunk s's TMA stores (X, and A_out when given) have read its slot.
+        // I: E and X staged through shared memory in 16-column chunks (NSL 2 KB slots per warp).
+        // The first NSL chunks are requested with TMA before the accumulator is ready; chunk s + NSL
+        // as soon as chunk s's TMA stores (X, and A_out when given) have read its slot.
         constexpr int CW = 16;
         constexpr int NSUB = HC / CW;
+        static_assert(NSUB >= NSL && (NSL & (NSL - 1)) == 0, "I epilogue: slots a power of two, <= chunks");
         constexpr uint32_t TILE = 32 * CW * 2;  // one 32-row operand tile (32-byte rows)
         const uint32_t ebase = saddr(smem + STAGES * STAGE_BYTES) + (warp - 2) * EPI_WARP_BYTES;
-        const uint32_t ebar = ebar0 + 16 * (warp - 2);
+        const uint32_t ebar = ebar0 + 8 * NSL * (warp - 2);
         uint32_t eph = 0, pending = 0;
         bool ok = true;
         for (int t = unit0; t < p.tiles && ok; t += units) {
@@ -680,9 +690,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const bool live = r0 < p.Mg;
           const int nw = n0 + c_lo;
           if (live && lane == 0) {
-            bulk_wait_read0();  // the previous tile's stores have read both slots
+            bulk_wait_read0();  // the previous tile's stores have read every slot
 #pragma unroll
-            for (int s = 0; s < 2; ++s) {
+            for (int s = 0; s < NSL; ++s) {
               if (nw + CW * s < p.Ng) {
                 epi_load_i(&tmE0, &tmE1, ebase + s * EPI_SLOT, ebar + 8 * s, TILE, nw + CW * s, r0, g);
                 pending |= 1u << s;
@@ -701,7 +711,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tmem_ld32(trow + c_lo + 32 * c, raw);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int sidx = 2 * c + h, slot = h;
+              const int sidx = 2 * c + h, slot = sidx & (NSL - 1);
               const int n = nw + CW * sidx;
               if (!live || n >= p.Ng || !ok) continue;
               if (!mbar_wait(ebar + 8 * slot, (eph >> slot) & 1u, abort_flag)) {
@@ -725,9 +735,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tma_store_3d(&tmE1, sb + TILE, n, r0, g);
                 if (p.aux2 != nullptr) tma_store_3d(&tmE2, sb, n, r0, g);
                 bulk_commit();
-                if (sidx + 2 < NSUB && n + 2 * CW < p.Ng) {
+                if (sidx + NSL < NSUB && n + NSL * CW < p.Ng) {
                   bulk_wait_read0();
-                  epi_load_i(&tmE0, &tmE1, sb, ebar + 8 * slot, TILE, n + 2 * CW, r0, g);
+                  epi_load_i(&tmE0, &tmE1, sb, ebar + 8 * slot, TILE, n + NSL * CW, r0, g);
                   pending |= 1u << slot;
                 }
               }
@@ -742,7 +752,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0) {
           // loads still in flight (only after an aborted wait) land before the CTA exits
 #pragma unroll
-          for (int s = 0; s < 2; ++s)
+          for (int s = 0; s < NSL; ++s)
             if ((pending >> s) & 1u) mbar_drain(ebar + 8 * s, (eph >> s) & 1u);
           bulk_wait0();
         }
@@ -1001,10 +1011,10 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
     }
   }
   constexpr int STAGE_BYTES = (TC_BM + BNL) * TC_BK * 2;
-  constexpr int STAGES = PAIR ? TC_STAGES_PAIR : TC_STAGES;
-  // barriers (2 per stage, 4 accumulator, 2 per epilogue warp), the TMEM slot and the abort word
-  constexpr int TAIL = ((2 * STAGES + 4 + 2 * TC_EPI_WARPS) * 8 + 8 + 255) / 256 * 256;
-  const int smem = STAGES * STAGE_BYTES + (EPI_STAGED ? EPI_BYTES : 0) + 1024 + TAIL;
+  constexpr int STAGES = tc_stages(MODE, PAIR);
+  // barriers (2 per stage, 4 accumulator, one per epilogue slot), the TMEM slot and the abort word
+  constexpr int TAIL = ((2 * STAGES + 4 + epi_slots(MODE, PAIR) * TC_EPI_WARPS) * 8 + 8 + 255) / 256 * 256;
+  const int smem = STAGES * STAGE_BYTES + (EPI_STAGED ? epi_bytes(MODE, PAIR) : 0) + 1024 + TAIL;
   auto kern = tc_gemm_kernel<T, ACT, MODE, BN, PAIR>;
   cudaError_t err = ensure_kernel_smem<tc_gemm_kernel<T, ACT, MODE, BN, PAIR>>(smem);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "tcgen05 kernel smem attribute: %s", cudaGetErrorString(err));

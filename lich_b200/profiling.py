@@ -1,0 +1,107 @@
+"""Per-operator CUDA-event timing inside running training steps.
+
+``operator_times(step, steps)`` runs ``step()`` ``steps`` times with every call of the fused GEMM
+entry point (``_native.fused_gemm``: P, I, W, ΔW and forward launches of the operator path) bracketed
+by CUDA events on the current stream, and groups the launches by operator and shape.  The kernels run
+back to back as in training, under the same clocks and power cap, so the rows add up to the step and
+show which operator falls behind the others (a wave-quantised grid, an epilogue-bound short
+reduction).  Event records between launches cost nothing measurable against millisecond kernels.
+
+    python -m lich_b200.profiling --config c5 [--batch 65536] [--steps 5]
+
+prints one row per (operator, M, K, B, groups) for the wide data-parallel step of configs[4] (dims
+(1000, 4096 x 6, 4096), bf16, tanh, T = 4) on one GPU.
+"""
+from __future__ import annotations
+
+import argparse
+import collections
+import statistics
+
+import torch
+
+from . import _native as N
+
+KIND = {N.MODE_PRED: "P", N.MODE_INFER: "I", N.MODE_WEIGHT: "W", N.MODE_WDELTA: "WD", N.MODE_FORWARD: "F"}
+
+
+def operator_times(step, steps: int = 5, warmup: int = 2) -> dict:
+    """Run ``warmup`` untimed and ``steps`` timed calls of ``step()``; return the step time and per
+    (operator, M, K, B, groups) the launches per step, median launch time, TFLOP/s and ms per step."""
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    rec = []
+    orig = N.fused_gemm
+
+    def timed(mode, *a, **k):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        orig(mode, *a, **k)
+        e1.record()
+        rec.append(((mode, k.get("M"), k.get("K"), k.get("B"), k.get("groups", 1)), e0, e1))
+
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    N.fused_gemm = timed
+    try:
+        s0.record()
+        for _ in range(steps):
+            step()
+        s1.record()
+        torch.cuda.synchronize()
+    finally:
+        N.fused_gemm = orig
+    by = collections.defaultdict(list)
+    for key, e0, e1 in rec:
+        by[key].append(e0.elapsed_time(e1))
+    rows = []
+    for (mode, M, K, B, G), ts in by.items():
+        med = statistics.median(ts)
+        rows.append({"op": KIND.get(mode, str(mode)), "M": M, "K": K, "B": B, "groups": G,
+                     "per_step": len(ts) / steps, "median_ms": round(med, 4),
+                     "tflops": round(2.0 * M * K * B * G / (med * 1e-3) / 1e12, 1),
+                     "ms_per_step": round(sum(ts) / steps, 3)})
+    rows.sort(key=lambda r: -r["ms_per_step"])
+    return {"step_ms": round(s0.elapsed_time(s1) / steps, 3),
+            "gemm_ms": round(sum(r["ms_per_step"] for r in rows), 3), "rows": rows}
+
+
+def _c5(batch: int):
+    from . import synthetic as S
+    from .data_parallel import DataParallelIPC
+    from .trainer import IPCConfig
+
+    dev = torch.device("cuda", 0)
+    dims = (1000,) + (4096,) * 6 + (4096,)
+    dt = torch.bfloat16
+    dp = DataParallelIPC(IPCConfig(dims=dims, alpha=1e-4, gamma=0.5, activation="tanh", dtype=dt), device=dev)
+    w0 = [w.to(dev, dt) for w in S.fan_in_normal(dims, seed=1)]
+    g = torch.Generator(device=dev).manual_seed(100)
+    x = torch.rand((dims[-1], batch), generator=g, device=dev).to(dt)
+    y = torch.zeros((dims[0], batch), device=dev, dtype=dt)
+    y.scatter_(0, torch.randint(0, dims[0], (1, batch), generator=g, device=dev), 1.0)
+
+    def step():
+        for w, s in zip(dp.model.w, w0):
+            w.copy_(s)
+        dp.train_step(x, y, T=4)
+    return step
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--config", choices=["c5"], default="c5")
+    ap.add_argument("--batch", type=int, default=65536)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args(argv)
+    res = operator_times(_c5(args.batch), steps=args.steps, warmup=args.warmup)
+    print(f"{'op':3s} {'M':>5s} {'K':>5s} {'B':>6s} {'G':>2s} {'/step':>5s} {'median ms':>9s} {'TF/s':>7s} {'ms/step':>8s}")
+    for r in res["rows"]:
+        print(f"{r['op']:3s} {r['M']:5d} {r['K']:5d} {r['B']:6d} {r['groups']:2d} {r['per_step']:5.0f} "
+              f"{r['median_ms']:9.3f} {r['tflops']:7.1f} {r['ms_per_step']:8.2f}")
+    print(f"step {res['step_ms']:.2f} ms, of which fused GEMM launches {res['gemm_ms']:.2f} ms")
+
+
+if __name__ == "__main__":
+    main()
