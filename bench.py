@@ -517,6 +517,19 @@ def run_c5(args, world, rank, local):
             "peak_kind": "sustained (kernels timed inside a ~0.1 s step)",
             "kernel": "tc_gemm_kernel (all GEMMs of the step; per-rank FLOP / per-step time, comms included)",
             "algorithmic_flop_per_step_per_rank": flop_rank}
+    # the dominant operator: CUDA events around every GEMM launch of one more untimed step (every rank
+    # runs it: the step's collectives), its per-launch FLOP / median launch time
+    from lich_b200.profiling import operator_times
+    ops = operator_times(lambda: (restore(), dp.train_step(*pool[0], T=T)), steps=1, warmup=0)
+    top = ops["rows"][0]
+    top_tfs = max_over_ranks(top["median_ms"], world, dev)
+    top_tfs = 2.0 * top["M"] * top["K"] * top["B"] * top["groups"] / (top_tfs * 1e-3) / 1e12
+    roof["dominant_kernel"] = {
+        "operator": f"{top['op']} M={top['M']} K={top['K']} B={top['B']} groups={top['groups']} "
+                    f"(tc_gemm_kernel, CTA pairs)",
+        "launches_per_step": top["per_step"], "median_launch_ms": top["median_ms"],
+        "share_of_step": round(top["ms_per_step"] / ops["step_ms"], 3),
+        "achieved": round(top_tfs, 1), "frac": round(top_tfs / pk["bf16_tflops_sustained"], 4)}
     # e2e: the public API with the batch in pinned host memory, copied in every step on a copy stream
     # (double-buffered: step i's copy overlaps step i-1), a metric read back every step
     x_h = pool[0][0].cpu().pin_memory()

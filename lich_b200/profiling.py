@@ -8,9 +8,11 @@ show which operator falls behind the others (a wave-quantised grid, an epilogue-
 reduction).  Event records between launches cost nothing measurable against millisecond kernels.
 
     python -m lich_b200.profiling --config c5 [--batch 65536] [--steps 5]
+    python -m lich_b200.profiling --gemm inference:4096:1000:65536 [--launches 3]
 
-prints one row per (operator, M, K, B, groups) for the wide data-parallel step of configs[4] (dims
-(1000, 4096 x 6, 4096), bf16, tanh, T = 4) on one GPU.
+The first prints one row per (operator, M, K, B, groups) for the wide data-parallel step of
+configs[4] (dims (1000, 4096 x 6, 4096), bf16, tanh, T = 4) on one GPU; the second times single
+launches of one operator on seeded operands (the case to give ncu).
 """
 from __future__ import annotations
 
@@ -88,13 +90,60 @@ def _c5(batch: int):
     return step
 
 
+def gemm_launches(kind: str, M: int, K: int, B: int, *, launches: int = 3, dtype=torch.bfloat16,
+                  act: str = "tanh") -> list[float]:
+    """Run one operator of the trainer's operator path (stored activations) ``launches`` times on seeded
+    operands and return each launch's milliseconds: a single-kernel case for ncu captures."""
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(M + K + B)
+
+    def r(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * scale).to(dtype)
+    mode = {"prediction": N.MODE_PRED, "inference": N.MODE_INFER, "weight": N.MODE_WEIGHT,
+            "wdelta": N.MODE_WDELTA, "forward": N.MODE_FORWARD}[kind]
+    if mode == N.MODE_PRED:
+        ops = (r(M, K, scale=K ** -0.5), r(K, B), r(M, B, scale=0.0), r(M, B), None)  # a, b, out, aux, aux2
+    elif mode == N.MODE_FORWARD:
+        ops = (r(M, K, scale=K ** -0.5), r(K, B), r(M, B, scale=0.0), None, r(M, B, scale=0.0))
+    elif mode == N.MODE_INFER:
+        ops = (r(K, M, scale=M ** -0.5), r(K, B, scale=0.5), r(M, B), r(M, B, scale=0.5), r(M, B, scale=0.0))
+    elif mode == N.MODE_WEIGHT:
+        ops = (r(M, B, scale=0.5), r(K, B), r(M, K, scale=0.05), None, None)
+    else:
+        ops = (r(M, B, scale=0.5), r(K, B), torch.zeros(M, K, device=dev), None, None)
+    a, b, out, aux, aux2 = ops
+    scale = 0.5 if mode == N.MODE_INFER else 1e-4
+    flags = N.FLAG_AOUT_STORED if mode == N.MODE_INFER else 0
+    times = []
+    for _ in range(launches):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        N.fused_gemm(mode, a, b, out, aux, aux2, M=M, K=K, B=B, scale=scale, flags=flags, act=act, dtype=dtype,
+                     device=dev)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    if N.device_status() != 0:
+        raise RuntimeError("device-side wait timed out")
+    return times
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--config", choices=["c5"], default="c5")
     ap.add_argument("--batch", type=int, default=65536)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--gemm", default="", help="kind:M:K:B -- time one operator's launches instead of a step")
+    ap.add_argument("--launches", type=int, default=3)
     args = ap.parse_args(argv)
+    if args.gemm:
+        kind, M, K, B = args.gemm.split(":")
+        M, K, B = int(M), int(K), int(B)
+        ts = gemm_launches(kind, M, K, B, launches=args.launches)
+        for t in ts:
+            print(f"{kind} {M} x {K} x {B}: {t:.4f} ms, {2.0 * M * K * B / (t * 1e-3) / 1e12:.1f} TF/s")
+        return
     res = operator_times(_c5(args.batch), steps=args.steps, warmup=args.warmup)
     print(f"{'op':3s} {'M':>5s} {'K':>5s} {'B':>6s} {'G':>2s} {'/step':>5s} {'median ms':>9s} {'TF/s':>7s} {'ms/step':>8s}")
     for r in res["rows"]:
