@@ -182,10 +182,6 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-// Bring `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2; no completion to wait for.
-__device__ __forceinline__ void prefetch_l2(const void* ptr, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
-}
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
@@ -690,28 +686,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t ebar = ebar0 + 8 * NSL * (warp - 2);
         uint32_t eph = 0, pending = 0;
         bool ok = true;
-        // L2 prefetch of a tile's E and X block (32 rows x HC columns per warp): each lane brings its
-        // row's whole segment of both, so the 32-byte-per-row TMA chunk loads that follow hit L2 rather
-        // than opening a DRAM page per row and chunk; issued a tile ahead (the first tile at once)
-        auto prefetch_ex = [&](int t) {
-          int g, m0, n0, sp;
-          tile_coords(p, t, BN, g, m0, n0, sp, TM, rank);
-          const int row = m0 + 32 * q + lane, col = n0 + c_lo;
-          if (row < p.Mg && col < p.Ng) {
-            const uint32_t bytes = (uint32_t)min(HC, p.Ng - col) * 2u;
-            const long long off = (long long)row * p.ld_out + col;
-            if (p.aux != nullptr) prefetch_l2(reinterpret_cast<const T*>(p.aux) + g * p.gs_aux + off, bytes);
-            prefetch_l2(reinterpret_cast<const T*>(p.out) + g * p.gs_out + off, bytes);
-          }
-        };
-        if (unit0 < p.tiles) prefetch_ex(unit0);
         for (int t = unit0; t < p.tiles && ok; t += units) {
           int g, m0, n0, sp;
           tile_coords(p, t, BN, g, m0, n0, sp, TM, rank);
           const int r0 = m0 + 32 * q;
           const bool live = r0 < p.Mg;
           const int nw = n0 + c_lo;
-          if (t + units < p.tiles) prefetch_ex(t + units);
           if (live && lane == 0) {
             bulk_wait_read0();  // the previous tile's stores have read every slot
 #pragma unroll
