@@ -535,7 +535,7 @@ def run_c5(args, world, rank, local):
     x_h = pool[0][0].cpu().pin_memory()
     y_h = pool[0][1].cpu().pin_memory()
     ring = [(torch.empty_like(pool[0][0]), torch.empty_like(pool[0][1])) for _ in range(2)]
-    n_e2e = max(3, min(args.steps, 8))
+    n_e2e = max(3, min(args.steps, 20))
     metric_h = torch.empty(n_e2e, dtype=torch.float32).pin_memory()
     copy = torch.cuda.Stream(dev)
     ready = [torch.cuda.Event() for _ in range(2)]
@@ -550,6 +550,13 @@ def run_c5(args, world, rank, local):
             ring[slot][1].copy_(y_h, non_blocking=True)
             ready[slot].record(copy)
 
+    # one untimed pass of the loop body first (copy stream, pinned-source copies, the metric read-back)
+    h2d(0)
+    stream.wait_event(ready[0])
+    restore()
+    dp.train_step(*ring[0], T=T)
+    free[0].record(stream)
+    metric_h[0:1].copy_((dp.model.e[0].float() ** 2).mean().reshape(1), non_blocking=True)
     barrier(world)
     torch.cuda.synchronize(dev)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

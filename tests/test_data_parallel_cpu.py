@@ -74,6 +74,9 @@ def _worker(rank, world, port, data, out, reduce):
             def _cap(self, leave):
                 caps.append(("cap", leave))
 
+            def _sms(self):
+                return 148
+
         caps = []
 
         w0, x, y = data
@@ -142,7 +145,9 @@ def test_delta_cap_saves_waves():
     assert dp._leave_for(1) == 20          # 256 tiles: 64 pairs -> 4 waves
     assert dp._leave_for(0) == 20          # 4 x 16 = 64 tiles: one wave on 64 pairs
     assert dp._leave_for(2) == 24          # 16 x 2 = 32 tiles: one wave already
-    fixed = DataParallelIPC(m.cfg, device=torch.device("cpu"), model=m, comm_sms=24)
+    fixed = DataParallelIPC(m.cfg, device=torch.device("cpu"), model=m, comm_sms=24, comm_sms_min=24)
     assert fixed._leave_for(1) == 24
+    default = DataParallelIPC(m.cfg, device=torch.device("cpu"), model=m, comm_sms=8)
+    assert default.comm_sms_min == 8
     with pytest.raises(ValueError):
         DataParallelIPC(m.cfg, device=torch.device("cpu"), model=m, comm_sms=24, comm_sms_min=30)
