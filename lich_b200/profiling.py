@@ -9,10 +9,12 @@ reduction).  Event records between launches cost nothing measurable against mill
 
     python -m lich_b200.profiling --config c5 [--batch 65536] [--steps 5]
     python -m lich_b200.profiling --gemm inference:4096:1000:65536 [--launches 3]
+    python -m lich_b200.profiling --net-launches
 
 The first prints one row per (operator, M, K, B, groups) for the wide data-parallel step of
 configs[4] (dims (1000, 4096 x 6, 4096), bf16, tanh, T = 4) on one GPU; the second times single
-launches of one operator on seeded operands (the case to give ncu).
+launches of one operator on seeded operands (the case to give ncu); the third splits the hidden-64
+persistent kernel's launch time into a fixed part and a per-step part.
 """
 from __future__ import annotations
 
@@ -128,6 +130,54 @@ def gemm_launches(kind: str, M: int, K: int, B: int, *, launches: int = 3, dtype
     return times
 
 
+def net_launch_costs(depth: int = 6, sizes=(1, 2, 4, 8, 20, 50, 100, 500), reps: int = 7) -> dict:
+    """The persistent kernel's cost per launch: median CUDA-event time of ``train_pool`` launches of
+    ``sizes`` steps (configs[1]: dims (10, 64 x depth, 784), B = 128, fp16, tanh, T = 4), each queued
+    behind a 200-step launch so the GPU is busy when it starts, the least-squares fit
+    fixed + per-step, and a 20-step launch that starts on an idle GPU (after a synchronize)."""
+    from . import synthetic as S
+    from .trainer import IPCConfig, TileLangIPC
+
+    dev = torch.device("cuda", 0)
+    dims = S.paper_dims(depth)
+    B, T, dt = 128, 4, torch.float16
+    m = TileLangIPC(IPCConfig(dims=dims, alpha=1e-4, gamma=0.5, activation="tanh", dtype=dt), device=dev)
+    w0 = [w.to(dev, dt) for w in S.fan_in_normal(dims, seed=1)]
+    g = torch.Generator(device=dev).manual_seed(5)
+    P = 256
+    px = torch.rand((P, dims[-1], B), generator=g, device=dev).to(dt)
+    lab = torch.randint(0, dims[0], (P, B), generator=g, device=dev)
+    py = torch.zeros((P, dims[0], B), device=dev, dtype=dt)
+    py.scatter_(1, lab.unsqueeze(1), 1.0)
+
+    def restore():
+        for d, s0 in zip(m.w, w0):
+            d.copy_(s0)
+
+    def timed(steps, idle, rep):
+        restore()
+        m.train_pool(px, py, steps=200, T=T)
+        if idle:
+            torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        m.train_pool(px, py, steps=steps, T=T, first_batch=rep)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3
+
+    for _ in range(3):
+        timed(500, False, 0)
+    busy = {n: statistics.median(timed(n, False, r) for r in range(reps)) for n in sizes}
+    xs, ys = list(busy), list(busy.values())
+    mx, my = sum(xs) / len(xs), sum(ys) / len(ys)
+    per = sum((a - mx) * (b - my) for a, b in zip(xs, ys)) / sum((a - mx) ** 2 for a in xs)
+    idle20 = statistics.median(timed(20, True, r) for r in range(reps))
+    return {"busy_us": {n: round(v, 1) for n, v in busy.items()}, "fixed_us": round(my - per * mx, 1),
+            "per_step_us": round(per, 2), "idle_20_step_launch_us": round(idle20, 1),
+            "busy_20_step_launch_us": busy.get(20)}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--config", choices=["c5"], default="c5")
@@ -136,7 +186,16 @@ def main(argv=None) -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--gemm", default="", help="kind:M:K:B -- time one operator's launches instead of a step")
     ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--net-launches", action="store_true",
+                    help="configs[1]: cost per persistent-kernel launch (fixed + per step, idle vs busy GPU)")
     args = ap.parse_args(argv)
+    if args.net_launches:
+        res = net_launch_costs()
+        for n, v in res["busy_us"].items():
+            print(f"{n:4d} steps per launch: {v:9.1f} us ({v / n:6.2f} us/step)")
+        print(f"fit: {res['fixed_us']} us per launch + {res['per_step_us']} us per step; 20-step launch "
+              f"on an idle GPU {res['idle_20_step_launch_us']} us, behind a busy one {res['busy_20_step_launch_us']} us")
+        return
     if args.gemm:
         kind, M, K, B = args.gemm.split(":")
         M, K, B = int(M), int(K), int(B)
