@@ -1175,8 +1175,9 @@ def main():
                     help="c5: SMs the delta GEMMs leave to the overlapped all-reduces (default: DataParallelIPC's)")
     ap.add_argument("--comm-sms-min", type=int, default=-1,
                     help="c5: fewest SMs a delta GEMM may leave when more CTAs save it a wave of tiles")
-    ap.add_argument("--dp-reduce", choices=["rs_ag", "allreduce"], default="rs_ag",
-                    help="c5: reduce-scatter + sliced apply + all-gather, or one all-reduce per layer")
+    ap.add_argument("--dp-reduce", choices=["rs_ag", "allreduce", "nvls"], default="rs_ag",
+                    help="c5: reduce-scatter + sliced apply + all-gather, one all-reduce per layer, or the "
+                         "delta GEMMs adding into an NVLS multicast buffer (fused dW + reduction)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

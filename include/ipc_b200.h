@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define IPC_ABI_VERSION 3
+#define IPC_ABI_VERSION 4
 
 /* return codes */
 #define IPC_OK 0
@@ -153,6 +153,21 @@ int ipc_forward(const void* x_up, const void* w, void* out, int M, int K, int B,
  * IPC_FLAG_ACCUMULATE adds into dw.  Without a workspace the tcgen05 kernel
  * serves calls without IPC_FLAG_ACTIVATE_B only (with it, ipc_fused_gemm_ws
  * below).  No single reference counterpart: it subsumes the entries above.
+ *
+ * IPC_FLAG_MULTIMEM_RED (WDELTA only; tensor-core shapes, 16-bit operands, a
+ * stored activation, no IPC_FLAG_ACCUMULATE): `out` is the multicast (NVLS)
+ * address of an fp32 buffer bound on every GPU of a group (for example the
+ * multicast_ptr of a torch symmetric-memory rendezvous).  The epilogue adds
+ * scale * acc into every GPU's copy through the NVSwitch
+ * (multimem.red.add.v4.f32), so the weight delta and its all-reduce are one
+ * kernel: the reduction traffic leaves each SM tile by tile while later tiles
+ * accumulate.  The caller zeroes every copy before the first rank's call and
+ * orders all ranks' calls before anyone reads the sum (e.g. a stream-ordered
+ * collective on a small tensor); each thread fences at system scope before the
+ * kernel ends.  The sum is identical on every GPU but not bitwise repeatable
+ * from run to run (the switch adds contributions in arrival order).  Other
+ * shapes return IPC_ERR_UNSUPPORTED.  Replaces the data-parallel ΔW
+ * reduce-scatter / all-gather; the reference is single-GPU.
  */
 #define IPC_MODE_PRED 0
 #define IPC_MODE_INFER 1
@@ -162,6 +177,7 @@ int ipc_forward(const void* x_up, const void* w, void* out, int M, int K, int B,
 #define IPC_FLAG_ACTIVATE_B 1
 #define IPC_FLAG_AOUT_STORED 2
 #define IPC_FLAG_ACCUMULATE 4
+#define IPC_FLAG_MULTIMEM_RED 8
 int ipc_fused_gemm(int mode, const void* a, const void* b, void* out, const void* aux, void* aux2, int M, int K,
                    int B, int groups, float scale, int flags, int act, int dtype, int algo, void* stream);
 

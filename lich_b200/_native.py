@@ -29,7 +29,7 @@ DTYPE_NAMES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": t
 ALGO_CODES = {"auto": 0, "simt": 1, "generic": 1, "tcgen05": 2, "outer": 3}
 
 MODE_PRED, MODE_INFER, MODE_WEIGHT, MODE_WDELTA, MODE_FORWARD = 0, 1, 2, 3, 4
-FLAG_ACTIVATE_B, FLAG_AOUT_STORED, FLAG_ACCUMULATE = 1, 2, 4
+FLAG_ACTIVATE_B, FLAG_AOUT_STORED, FLAG_ACCUMULATE, FLAG_MULTIMEM_RED = 1, 2, 4, 8
 
 # Split-K scratch that covers every shape the weight update splits: a split happens only with fewer
 # than half the SMs' worth of 128 x 128 output tiles, and splits x tiles stays below 148 + tiles, so the
@@ -166,8 +166,11 @@ def stream_handle(device: torch.device | None = None) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-def ptr(t: torch.Tensor | None) -> int | None:
-    return None if t is None else t.data_ptr()
+def ptr(t: "torch.Tensor | int | None") -> int | None:
+    """A tensor's device address; an int is taken as an address already (a multicast pointer)."""
+    if t is None or isinstance(t, int):
+        return t
+    return t.data_ptr()
 
 
 def act_code(name: str) -> int:
@@ -194,6 +197,18 @@ def torch_dtype(dtype) -> torch.dtype:
             raise ValueError(f"Unsupported dtype {dtype!r}")
         return DTYPE_NAMES[dtype]
     return dtype
+
+
+def tc_eligible(mode: int, M: int, K: int, B: int, dtype) -> bool:
+    """Whether ``ipc_fused_gemm`` (IPC_ALGO_AUTO, stored operand, no workspace) takes the tcgen05 kernel
+    for this shape: the rule of ``tc_eligible`` in csrc/ipc_tc.cu (16-bit operands, every extent a
+    multiple of 8, at least 64 x 128 x 64 and 128 x 256 x 256 multiply-adds)."""
+    if torch_dtype(dtype) not in (torch.float16, torch.bfloat16):
+        return False
+    if M % 8 or K % 8 or B % 8:
+        return False
+    Mg, Ng, Kg = (M, K, B) if mode in (MODE_WEIGHT, MODE_WDELTA) else (M, B, K)
+    return Mg >= 64 and Ng >= 128 and Kg >= 64 and Mg * Ng * Kg >= 128 * 256 * 256
 
 
 def net_plan(dims, B: int, nets: int = 1, cluster: int = 0) -> tuple[int, int] | None:

@@ -303,6 +303,23 @@ static int fused_gemm_impl(int mode, const void* a, const void* b, void* out, co
   p.a_out_from_stored = (flags & IPC_FLAG_AOUT_STORED) != 0;
   p.groups = groups;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (flags & IPC_FLAG_MULTIMEM_RED) {
+    // the weight delta added into a multicast buffer on every GPU of a group: tcgen05 staged epilogue only
+    IPC_REQUIRE(mode == MODE_WD, "IPC_FLAG_MULTIMEM_RED applies to IPC_MODE_WDELTA only");
+    IPC_REQUIRE(!p.accumulate && !bact, "IPC_FLAG_MULTIMEM_RED excludes IPC_FLAG_ACCUMULATE and IPC_FLAG_ACTIVATE_B");
+    if (M == 0 || K == 0) return IPC_OK;
+    IPC_REQUIRE(out && (B == 0 || (a && b)), "null operand pointer");
+    if (B == 0 || algo == IPC_ALGO_SIMT || algo == IPC_ALGO_OUTER ||
+        !tc_eligible(mode, M, K, B, dtype, algo, false, false))
+      return set_error(IPC_ERR_UNSUPPORTED, "IPC_FLAG_MULTIMEM_RED: M=%d K=%d B=%d dtype=%d is not a tcgen05 weight delta",
+                       M, K, B, dtype);
+    p.A = a; p.lda = B; p.gsA = (long long)M * B;
+    p.Bm = b; p.ldb = B; p.gsB = (long long)K * B;
+    p.Mg = M; p.Ng = K; p.Kg = B;
+    p.out = out; p.gsOut = (long long)M * K;
+    p.mcast = 1;
+    return launch_tc(p, mode, act, dtype, s, nullptr, 0, tune);
+  }
   if (mode == MODE_W || mode == MODE_WD) {
     if (M == 0 || K == 0) return IPC_OK;
     IPC_REQUIRE(out && (B == 0 || (a && b)), "null operand pointer");

@@ -62,6 +62,7 @@ struct GemmArgs {
   int accumulate;   // WD
   int a_out_from_stored;  // I: A_out = f(cast(x_new)) (what recompute mode reads back) instead of f(x_new)
   OptParams opt;    // WO: the optimizer step applied to W
+  int mcast;        // WD: out is a multicast (NVLS) address, the epilogue adds with multimem.red
 };
 
 int launch_generic(const GemmArgs& p, int mode, bool bact, int act, int dtype, cudaStream_t s);

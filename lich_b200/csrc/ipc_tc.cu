@@ -99,6 +99,7 @@ struct TcParams {
   // WD on CTA pairs: the two batch halves of a tile (splits == 2) are added into a zeroed dw with fp32
   // vector atomics; 0 + a + b == 0 + b + a exactly, so the result does not depend on their order
   int atomic;
+  int mcast;  // WD: out is a multicast (NVLS) address; the epilogue adds into every GPU's copy
   int raster;  // M-tiles per raster band of the tile walk
   OptParams opt;  // WO: optimizer step applied to W in the epilogue
 };
@@ -180,6 +181,7 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
@@ -676,8 +678,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (staged) {
       if constexpr (MODE == MODE_I) {
         // I: E and X staged through shared memory in 16-column chunks (NSL 2 KB slots per warp).
-        // The first NSL chunks are requested with TMA before the accumulator is ready; chunk s + NSL
-        // as soon as chunk s's TMA stores (X, and A_out when given) have read its slot.
+        // The first NSL chunks are requested with TMA before the accumulator is ready; later chunks as
+        // the TMA stores (X, and A_out when given) of the chunk before free its slot.
         constexpr int CW = 16;
         constexpr int NSUB = HC / CW;
         static_assert(NSUB >= NSL && (NSL & (NSL - 1)) == 0, "I epilogue: slots a power of two, <= chunks");
@@ -738,10 +740,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tma_store_3d(&tmE1, sb + TILE, n, r0, g);
                 if (p.aux2 != nullptr) tma_store_3d(&tmE2, sb, n, r0, g);
                 bulk_commit();
-                if (sidx + NSL < NSUB && n + NSL * CW < p.Ng) {
-                  bulk_wait_read0();
-                  epi_load_i(&tmE0, &tmE1, sb, ebar + 8 * slot, TILE, n + NSL * CW, r0, g);
-                  pending |= 1u << slot;
+                // refill: with two slots, this chunk's slot once its stores have read it; with more, the
+                // previous chunk's slot, whose stores were issued a chunk earlier (waiting on all but the
+                // newest store group keeps this chunk's stores off the critical path)
+                constexpr int D = NSL >= 3 ? 1 : 0;
+                const int rs = sidx - D;
+                if (rs >= 0 && rs + NSL < NSUB && nw + CW * (rs + NSL) < p.Ng) {
+                  if constexpr (D == 1) bulk_wait_read1(); else bulk_wait_read0();
+                  const int rslot = rs & (NSL - 1);
+                  epi_load_i(&tmE0, &tmE1, ebase + rslot * EPI_SLOT, ebar + 8 * rslot, TILE, nw + CW * (rs + NSL),
+                             r0, g);
+                  pending |= 1u << rslot;
                 }
               }
               __syncwarp();
@@ -798,7 +807,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               const uint4 v = lds128(xb + r * 128 + ((cj ^ (r & 7)) << 4));
               if (r0 + r < p.Mg && n < p.Ng) {
                 float* o = dst + g * p.gs_out + (long long)(r0 + r) * p.ld_out + n;
-                if (p.atomic)
+                if (p.mcast)
+                  asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(o),
+                               "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+                               "f"(__uint_as_float(v.w))
+                               : "memory");
+                else if (p.atomic)
                   atomicAdd(reinterpret_cast<float4*>(o), make_float4(__uint_as_float(v.x), __uint_as_float(v.y),
                                                                       __uint_as_float(v.z), __uint_as_float(v.w)));
                 else
@@ -809,6 +823,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
           if (++acc == 2) { acc = 0; aphase ^= 1; }
         }
+        // multicast adds performed at system scope before the kernel ends (the caller's cross-GPU
+        // ordering starts from this kernel's completion)
+        if (p.mcast) asm volatile("fence.acq_rel.sys;" ::: "memory");
       }
     } else {
       for (int t = unit0; t < p.tiles; t += units) {
@@ -1005,6 +1022,7 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   // zeroed first, where the half tiles fill the last wave (4096^2 = 256 pair tiles on 74 pairs: 4 waves,
   // 3.5 with halves); taken for a saving of >= 5 % of the tile time (or on request, tc_splits >= 2)
   p.atomic = 0;
+  p.mcast = a.mcast;
   if (MODE == MODE_WD && PAIR && !a.accumulate && want != 1 && nk >= 16 && a.gsOut == (long long)a.Mg * a.Ng) {
     const long long units = cap / 2 > 0 ? cap / 2 : 1;
     const long long w1 = (p.tiles + units - 1) / units, w2 = (2LL * p.tiles + units - 1) / units;
@@ -1040,7 +1058,7 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   auto kern = tc_gemm_kernel<T, ACT, MODE, BN, PAIR>;
   cudaError_t err = ensure_kernel_smem<tc_gemm_kernel<T, ACT, MODE, BN, PAIR>>(smem);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "tcgen05 kernel smem attribute: %s", cudaGetErrorString(err));
-  if (p.atomic) {  // the two halves of each tile add into zeros
+  if (p.atomic && !p.mcast) {  // the two halves of each tile add into zeros (a multicast dw: the caller's)
     err = cudaMemsetAsync(a.out, 0, (size_t)a.groups * a.Mg * a.Ng * sizeof(float), s);
     if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "dw zero fill: %s", cudaGetErrorString(err));
   }
@@ -1135,7 +1153,10 @@ int launch_tc(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, f
   const uintptr_t mis = reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.Bm) |
                         reinterpret_cast<uintptr_t>(a.out) | reinterpret_cast<uintptr_t>(a.aux) |
                         reinterpret_cast<uintptr_t>(a.aux2);
-  if (mis & 15) return launch_generic(a, mode, false, act, dtype, s);
+  if (mis & 15) {
+    if (a.mcast) return set_error(IPC_ERR_ARG, "IPC_FLAG_MULTIMEM_RED: operands must be 16-byte aligned");
+    return launch_generic(a, mode, false, act, dtype, s);
+  }
   // Tile width: the persistent walk takes ceil(tiles / CTAs) waves of one tile time each.  A 128 x 128
   // tile takes about 0.81 of a 128 x 256 tile's time (measured on B200 at 4096^2 x 65536: the MMAs are
   // bound by shared-memory operand reads, and the wide tile reads a third less per FLOP), so a tile

@@ -57,18 +57,24 @@ class DataParallelIPC:
 
     def __init__(self, cfg: IPCConfig, *, device: torch.device, group=None, seed: int = 0,
                  model: TileLangIPC | None = None, comm_sms: int = 24, comm_sms_min: int | None = None,
-                 reduce: str = "rs_ag"):
+                 reduce: str = "rs_ag", keep_delta: bool = False):
         """comm_sms: SMs the delta GEMMs leave to the reductions they overlap (world > 1).
         comm_sms_min: a delta GEMM may leave as few as this many SMs (default min(16, comm_sms)) when the
         extra CTAs save it a wave of output tiles (e.g. 4096 x 4096 = 256 tiles of 256 x 256: 5 waves on
         62 CTA pairs, 4 on 64; measured at 2 GPUs on configs[4]: 1.8 % faster steps than a fixed 24).
-        reduce: "rs_ag" (reduce-scatter, sliced apply, all-gather) or "allreduce"."""
+        reduce: "rs_ag" (reduce-scatter, sliced apply, all-gather), "allreduce", or "nvls": the delta
+        GEMMs add their fp32 dW straight into a multicast buffer on every GPU through the NVSwitch
+        (IPC_FLAG_MULTIMEM_RED), a one-word collective orders the ranks, and every rank applies the
+        whole sum -- no NCCL traffic and no SMs held back; it falls back to "rs_ag" on every rank when
+        any rank has no multicast support or a layer is not a tensor-core weight delta.
+        keep_delta: "nvls" only -- also copy each step's summed fp32 dW into ``_dw`` (one extra pass
+        over it; the other forms leave their part of the sum there anyway)."""
         if comm_sms < 0:
             raise ValueError("comm_sms must be >= 0")
         comm_sms_min = min(16, comm_sms) if comm_sms_min is None else int(comm_sms_min)
         if not 0 <= comm_sms_min <= comm_sms:
             raise ValueError("comm_sms_min must be in [0, comm_sms]")
-        if reduce not in ("rs_ag", "allreduce"):
+        if reduce not in ("rs_ag", "allreduce", "nvls"):
             raise ValueError(f"unknown reduce {reduce!r}")
         self.group = group
         self.comm_sms = int(comm_sms)
@@ -82,6 +88,70 @@ class DataParallelIPC:
             for w in self.model.w:  # identical replicas to start from
                 dist.broadcast(w, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
         self._dw = self._alloc_deltas()
+        self.keep_delta = bool(keep_delta)
+        self._mc = None          # "nvls": two (symmetric tensor, handle) pairs, alternated per step
+        self._mc_step = 0
+        self._mc_ok: dict = {}   # local batch -> every rank can take the multicast path
+        if self.reduce == "nvls" and self.world > 1 and not self._setup_multicast():
+            self.reduce = "rs_ag"
+
+    def _agree(self, ok: bool) -> bool:
+        """True on every rank iff ``ok`` on every rank (a MIN all-reduce of one word)."""
+        dev = self.model.w[0].device
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+        return bool(flag.item())
+
+    def _setup_multicast(self) -> bool:
+        """Two fp32 dW buffers in symmetric memory, each with an NVLS multicast mapping, zeroed on every
+        GPU; False (on every rank) when any rank cannot have them."""
+        bufs = []
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+            n = sum(t.numel() for t in self._dw)
+            grp = self.group if self.group is not None else dist.group.WORLD
+            for _ in range(2):
+                t = symm_mem.empty(n, dtype=torch.float32, device=self.model.w[0].device)
+                h = symm_mem.rendezvous(t, grp)
+                bufs.append((t, h))
+            ok = all(int(h.multicast_ptr) != 0 for _, h in bufs)
+        except Exception:  # no symmetric memory / multicast on this device or backend
+            ok = False
+        if not self._agree(ok):
+            return False
+        for t, _ in bufs:
+            t.zero_()
+        torch.cuda.synchronize(self.model.w[0].device)
+        dist.barrier(group=self.group)
+        self._mc = bufs
+        self._offsets = []
+        off = 0
+        for t in self._dw:
+            self._offsets.append(off)
+            off += t.numel()
+        self._sync_word = torch.zeros(1, dtype=torch.float32, device=self.model.w[0].device)
+        return True
+
+    def _multicast_ok(self, B: int) -> bool:
+        """Whether every layer's delta is a tensor-core weight delta on every rank at local batch B."""
+        if B not in self._mc_ok:
+            m, d = self.model, self.cfg.dims
+            ok = m._ac is not None and self.cfg.dtype in (torch.float16, torch.bfloat16) and all(
+                N.tc_eligible(N.MODE_WDELTA, d[l], d[l + 1], B, self.cfg.dtype) for l in range(len(d) - 1))
+            self._mc_ok[B] = self._agree(ok)
+        return self._mc_ok[B]
+
+    def _deltas_multicast(self, order, B: int) -> torch.Tensor:
+        """Every layer's dW added into this step's multicast buffer on every GPU; returns the local copy."""
+        m, d = self.model, self.cfg.dims
+        t, h = self._mc[self._mc_step & 1]
+        base = int(h.multicast_ptr)
+        for l in order:
+            kc = m._kernel_config("weight", d[l], d[l + 1], B)
+            N.fused_gemm(N.MODE_WDELTA, m.e[l], m._ac[l + 1], base + 4 * self._offsets[l], M=d[l], K=d[l + 1],
+                         B=B, scale=self.cfg.alpha, flags=N.FLAG_MULTIMEM_RED, act=self.cfg.activation,
+                         dtype=self.cfg.dtype, device=m.device, tune=kc.tune())
+        return t
 
     def _alloc_deltas(self) -> list[torch.Tensor]:
         d = self.cfg.dims
@@ -186,6 +256,25 @@ class DataParallelIPC:
         mark("inference")
         L = len(self.cfg.dims) - 1
         order = sorted(range(L), key=lambda l: -self._dw[l].numel())  # biggest reductions start first
+        B = int(m.x[0].shape[1])
+        if self._mc is not None and self._multicast_ok(B):
+            t = self._deltas_multicast(order, B)
+            mark("deltas")
+            # every rank's adds are in every copy: one stream-ordered word all-reduce (its kernels start
+            # after this rank's delta kernels, whose adds were fenced at system scope)
+            dist.all_reduce(self._sync_word, group=self.group)
+            for l in order:
+                off = self._offsets[l]
+                self._apply(l, t[off:off + self._dw[l].numel()].view_as(self._dw[l]))
+            if self.keep_delta:
+                for l in order:
+                    off = self._offsets[l]
+                    self._dw[l].view(-1).copy_(t[off:off + self._dw[l].numel()])
+            t.zero_()  # reused two steps on, after every rank has passed the next step's word all-reduce
+            self._mc_step += 1
+            mark("end")
+            m.steps_done += 1
+            return
         handles, gathers, pending = {}, [], []
 
         def finish(l):

@@ -26,7 +26,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in include/ipc_b200.h but not exported"
     assert set(N.EXPORTED) == set(declared)
-    assert lib.ipc_abi_version() == 3
+    assert lib.ipc_abi_version() == 4
 
 
 def test_abi_rejects_bad_arguments_without_a_gpu():
