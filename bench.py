@@ -505,10 +505,15 @@ def run_c5(args, world, rank, local):
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
     assert N.device_status() == 0
     # one more (untimed) step with phase marks: where the per-rank step time goes
-    marks: list = []
-    restore()
-    dp.train_step(*pool[0], T=T, phases=marks)
-    breakdown = {k: round(max_over_ranks(v, world, dev), 3) for k, v in dp.phase_times(marks).items()}
+    # three more (untimed) steps with phase marks, back to back: the median of each phase
+    runs = []
+    for i in range(3):
+        marks: list = []
+        restore()
+        dp.train_step(*pool[i % 2], T=T, phases=marks)
+        runs.append(marks)
+    per = [dp.phase_times(mk) for mk in runs]
+    breakdown = {k: round(max_over_ranks(statistics.median(p_[k] for p_ in per), world, dev), 3) for k in per[0]}
     flop_rank, bytes_rank = step_costs(dims, B, T, 2)
     pk = peaks()
     tfs = flop_rank / (ms / args.steps * 1e-3) / 1e12
