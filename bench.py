@@ -496,21 +496,26 @@ def run_c5(args, world, rank, local):
     with ClockSampler(local) as clk:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
+        h0 = time.perf_counter()
         for i in range(args.steps):
             step(i)
+        host_ms = (time.perf_counter() - h0) * 1e3  # issuing the K steps (the GPU runs behind)
         e1.record(stream)
         torch.cuda.synchronize(dev)
     barrier(world)
     launches = N.launch_count() - launches0
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    host_ms = max_over_ranks(host_ms, world, dev)
     assert N.device_status() == 0
     # one more (untimed) step with phase marks: where the per-rank step time goes
     # three more (untimed) steps with phase marks, back to back: the median of each phase
-    runs = []
+    runs, issue = [], []
     for i in range(3):
         marks: list = []
         restore()
+        h0 = time.perf_counter()
         dp.train_step(*pool[i % 2], T=T, phases=marks)
+        issue.append((time.perf_counter() - h0) * 1e3)  # the host's cost of issuing one step
         runs.append(marks)
     per = [dp.phase_times(mk) for mk in runs]
     breakdown = {k: round(max_over_ranks(statistics.median(p_[k] for p_ in per), world, dev), 3) for k in per[0]}
@@ -589,6 +594,8 @@ def run_c5(args, world, rank, local):
                    "comm_sms_min": dp.comm_sms_min if world > 1 else 0,
                    "dp_reduce": dp.reduce if world > 1 else None,
                    "step_breakdown_ms": breakdown,
+                   "host_issue_ms_per_step": round(host_ms / args.steps, 3),
+                   "host_ms_one_step": round(max_over_ranks(min(issue), world, dev), 3),
                    "l2": "inputs larger than L2 (the per-step state is GBs)"},
         "roofline": roof,
         "e2e": {"value": round(n_e2e * Bg / (ms_e2e * 1e-3), 1), "unit": "samples/s",
