@@ -64,14 +64,22 @@ constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;  // TMA warp + MMA warp + epi
 constexpr long long TC_WAIT_NS = 2000000000LL;
 
 // Epilogue staging through shared memory (P, W, F, WD, I without split-K).  P / W / F / WD use 4 KB
-// per epilogue warp as one 32-row x 128-byte transpose buffer; I uses 2 KB slots, each holding an E
-// tile and an X tile of 32 rows x 16 columns (32-byte rows, TMA 32-byte swizzle): two per warp, or
-// four in the CTA-pair form, which gives the mainloop one stage less (5 x 32 KB) so that an I epilogue
-// keeps three chunks' loads in flight -- the epilogue streams four operands (E, X in; X, A_out out)
-// and bounds the kernel when the reduction is short (K = 1000: a tile's MMAs take ~7 us).
+// per epilogue warp as one 32-row x 128-byte transpose buffer; I uses two slots per warp, each holding
+// an E tile and an X tile of 32 rows: 16 columns (2 KB slots) in the single-CTA form, 32 columns
+// (4 KB slots, 64-byte rows) in the CTA-pair form, whose mainloop then has one stage less (5 x 32 KB).
+// The I epilogue streams four operands (E, X in; X, A_out out) and bounds the kernel when the
+// reduction is short (K = 1000: a tile's MMAs take ~7 us).
 constexpr int EPI_SLOT = 2048;
-__host__ __device__ constexpr int epi_slots(int mode, int pair) { return (mode == MODE_I && pair) ? 4 : 2; }
-__host__ __device__ constexpr int epi_warp_bytes(int mode, int pair) { return epi_slots(mode, pair) * EPI_SLOT; }
+// I epilogue chunk width: 16 columns (32-byte rows) in the single-CTA form, 32 (64-byte rows, whole
+// DRAM bursts per row) in the pair form; a slot holds the E and the X tile of one chunk
+__host__ __device__ constexpr int epi_cw(int pair) { return pair ? 32 : 16; }
+__host__ __device__ constexpr int epi_slot_bytes(int mode, int pair) {
+  return mode == MODE_I ? 2 * 32 * epi_cw(pair) * 2 : EPI_SLOT;
+}
+__host__ __device__ constexpr int epi_slots(int mode, int pair) { return 2; }
+__host__ __device__ constexpr int epi_warp_bytes(int mode, int pair) {
+  return epi_slots(mode, pair) * epi_slot_bytes(mode, pair);
+}
 __host__ __device__ constexpr int epi_bytes(int mode, int pair) { return TC_EPI_WARPS * epi_warp_bytes(mode, pair); }
 __host__ __device__ constexpr int tc_stages(int mode, int pair) {
   return pair ? (mode == MODE_I ? TC_STAGES_PAIR - 1 : TC_STAGES_PAIR) : TC_STAGES;
@@ -677,13 +685,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     } else if (staged) {
       if constexpr (MODE == MODE_I) {
-        // I: E and X staged through shared memory in 16-column chunks (NSL 2 KB slots per warp).
-        // The first NSL chunks are requested with TMA before the accumulator is ready; later chunks as
-        // the TMA stores (X, and A_out when given) of the chunk before free its slot.
-        constexpr int CW = 16;
+        // I: E and X staged through shared memory in CW-column chunks (NSL slots per warp, each an E
+        // and an X tile of 32 rows).  The first NSL chunks are requested with TMA before the
+        // accumulator is ready; later chunks as the TMA stores (X, and A_out when given) of the chunk
+        // before free its slot.  Rows of CW x 2 bytes: 32 (32-byte swizzle) or 64 (64-byte swizzle).
+        constexpr int CW = epi_cw(PAIR);
+        constexpr int CPL = 32 / CW;            // chunks per 32-column TMEM load
+        constexpr int VPR = CW / 8;             // 16-byte vectors per row
         constexpr int NSUB = HC / CW;
         static_assert(NSUB >= NSL && (NSL & (NSL - 1)) == 0, "I epilogue: slots a power of two, <= chunks");
-        constexpr uint32_t TILE = 32 * CW * 2;  // one 32-row operand tile (32-byte rows)
+        constexpr uint32_t TILE = 32 * CW * 2;  // one 32-row operand tile
+        constexpr uint32_t SLOT = epi_slot_bytes(MODE, PAIR);
+        auto swz = [&](int row) { return CW == 16 ? ((row >> 2) & 1) : ((row >> 1) & 3); };
         const uint32_t ebase = saddr(smem + STAGES * STAGE_BYTES) + (warp - 2) * EPI_WARP_BYTES;
         const uint32_t ebar = ebar0 + 8 * NSL * (warp - 2);
         uint32_t eph = 0, pending = 0;
@@ -699,7 +712,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
             for (int s = 0; s < NSL; ++s) {
               if (nw + CW * s < p.Ng) {
-                epi_load_i(&tmE0, &tmE1, ebase + s * EPI_SLOT, ebar + 8 * s, TILE, nw + CW * s, r0, g);
+                epi_load_i(&tmE0, &tmE1, ebase + s * SLOT, ebar + 8 * s, TILE, nw + CW * s, r0, g);
                 pending |= 1u << s;
               }
             }
@@ -715,8 +728,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             uint32_t raw[32];
             tmem_ld32(trow + c_lo + 32 * c, raw);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int sidx = 2 * c + h, slot = sidx & (NSL - 1);
+            for (int h = 0; h < CPL; ++h) {
+              const int sidx = CPL * c + h, slot = sidx & (NSL - 1);
               const int n = nw + CW * sidx;
               if (!live || n >= p.Ng || !ok) continue;
               if (!mbar_wait(ebar + 8 * slot, (eph >> slot) & 1u, abort_flag)) {
@@ -725,12 +738,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               }
               eph ^= 1u << slot;
               pending &= ~(1u << slot);
-              const uint32_t sb = ebase + slot * EPI_SLOT;
+              const uint32_t sb = ebase + slot * SLOT;
 #pragma unroll
-              for (int j = 0; j < 2; ++j) {  // 32-byte rows, 32-byte swizzle: vector j ^ ((row >> 2) & 1)
-                const uint32_t off = lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
+              for (int j = 0; j < VPR; ++j) {  // row = lane; TMA swizzle: vector j ^ swz(row)
+                const uint32_t off = lane * (CW * 2) + ((j ^ swz(lane)) << 4);
                 uint4 xv = lds128(sb + TILE + off), av;
-                epi_vec_i<T, ACT>(lds128(sb + off), xv, av, raw + 16 * h + 8 * j, p.scale, p.a_out_from_stored);
+                epi_vec_i<T, ACT>(lds128(sb + off), xv, av, raw + CW * h + 8 * j, p.scale, p.a_out_from_stored);
                 sts128(sb + TILE + off, xv);
                 if (p.aux2 != nullptr) sts128(sb + off, av);
               }
@@ -748,8 +761,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (rs >= 0 && rs + NSL < NSUB && nw + CW * (rs + NSL) < p.Ng) {
                   if constexpr (D == 1) bulk_wait_read1(); else bulk_wait_read0();
                   const int rslot = rs & (NSL - 1);
-                  epi_load_i(&tmE0, &tmE1, ebase + rslot * EPI_SLOT, ebar + 8 * rslot, TILE, nw + CW * (rs + NSL),
-                             r0, g);
+                  epi_load_i(&tmE0, &tmE1, ebase + rslot * SLOT, ebar + 8 * rslot, TILE, nw + CW * (rs + NSL), r0,
+                             g);
                   pending |= 1u << rslot;
                 }
               }
@@ -1046,7 +1059,8 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
     const long long gs[3] = {a.gsAux, a.gsOut, a.gsAux2};
     for (int i = 0; i < 3; ++i) {
       if (src[i] == nullptr) continue;
-      rc = make_map(&te[i], src[i], dtype, a.Ng, a.Mg, a.groups, a.Ng, gs[i], 16, 32, CU_TENSOR_MAP_SWIZZLE_32B);
+      rc = make_map(&te[i], src[i], dtype, a.Ng, a.Mg, a.groups, a.Ng, gs[i], epi_cw(PAIR), 32,
+                    PAIR ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
       if (rc) return rc;
     }
   }
