@@ -67,8 +67,7 @@ class BatchPipeline:
         if b.ndim == 1:  # images + labels
             B, F = int(a.shape[0]), int(a[0].numel())
             return {"kind": "images", "key": ("images", B, F, a.dtype),
-                    "a_h": torch.empty((S, B, F), dtype=a.dtype).pin_memory(),
-                    "b_h": torch.empty((S, B), dtype=torch.int64).pin_memory(),
+                    "a_h": None, "b_h": None, "h_shapes": ((S, B, F), a.dtype, (S, B), torch.int64),
                     "a_d": torch.empty((S, B, F), dtype=a.dtype, device=dev),
                     "b_d": torch.empty((S, B), dtype=torch.int64, device=dev),
                     "x": torch.empty((S, F, B), dtype=self.dtype, device=dev),
@@ -77,9 +76,17 @@ class BatchPipeline:
         x = torch.empty((S, F, B), dtype=self.dtype, device=dev)
         y = torch.empty((S, self.num_classes, B), dtype=self.dtype, device=dev)
         return {"kind": "prepared", "key": ("prepared", B, F, a.dtype),
-                "a_h": torch.empty((S, F, B), dtype=self.dtype).pin_memory(),
-                "b_h": torch.empty((S, self.num_classes, B), dtype=self.dtype).pin_memory(),
+                "a_h": None, "b_h": None,
+                "h_shapes": ((S, F, B), self.dtype, (S, self.num_classes, B), self.dtype),
                 "a_d": x, "b_d": y, "x": x, "y": y}
+
+    @staticmethod
+    def _staging(slot: dict) -> None:
+        """The slot's pinned staging buffers, allocated on first need (pinned sources never need them)."""
+        if slot["a_h"] is None:
+            sa, da, sb, db = slot["h_shapes"]
+            slot["a_h"] = torch.empty(sa, dtype=da).pin_memory()
+            slot["b_h"] = torch.empty(sb, dtype=db).pin_memory()
 
     def _take(self) -> list:
         """The host items of the next slot: ``per_slot`` batches, or one pool chunk (3-D x and y)."""
@@ -121,24 +128,26 @@ class BatchPipeline:
         pool = b0.ndim == 3
         n = int(a0.shape[0]) if pool else len(items)
         srcs = []
+        sa, _, sb, _ = slot["h_shapes"]
         for j, (a, b) in enumerate(items):
             if slot["kind"] == "images":
                 a = a.reshape(a.shape[0], -1)
-                if tuple(a.shape) != tuple(slot["a_h"].shape[1:]) or tuple(b.shape) != (slot["a_h"].shape[1],):
+                if tuple(a.shape) != tuple(sa[1:]) or tuple(b.shape) != (sa[1],):
                     raise ValueError("every batch of a pipeline must have the same shape")
                 b = b.to(torch.int64)
             else:
-                if tuple(a.shape[-2:]) != tuple(slot["a_h"].shape[1:]) or \
-                        tuple(b.shape[-2:]) != tuple(slot["b_h"].shape[1:]):
+                if tuple(a.shape[-2:]) != tuple(sa[1:]) or tuple(b.shape[-2:]) != tuple(sb[1:]):
                     raise ValueError("every batch of a pipeline must have the same shape")
                 if a.dtype != self.dtype or b.dtype != self.dtype:
                     raise ValueError("prepared batches must already be in the pipeline dtype")
-            dst_a = slot["a_h"][:n] if pool else slot["a_h"][j]
-            dst_b = slot["b_h"][:n] if pool else slot["b_h"][j]
             if not (a.is_pinned() and a.is_contiguous()):
+                self._staging(slot)
+                dst_a = slot["a_h"][:n] if pool else slot["a_h"][j]
                 dst_a.copy_(a)
                 a = dst_a
             if not (b.is_pinned() and b.is_contiguous()):
+                self._staging(slot)
+                dst_b = slot["b_h"][:n] if pool else slot["b_h"][j]
                 dst_b.copy_(b)
                 b = dst_b
             srcs.append((a, b))
