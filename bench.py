@@ -923,7 +923,8 @@ def run_c4a(args, world, rank, local):
         "config": {"workload": f"configs[3] small batch: dims (10,1024x4,784), B={B}, T=8, tanh, bf16 storage / "
                                f"fp32 accumulation, alpha 1e-4, gamma 0.5", "batch": B, "T": T,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "l2": "weights (8.4 MB) stay in L2 between phases; no flush (the step re-reads them 80 times)",
+                   "l2": "weights (8.4 MB) resident in the CTAs' shared memory for the launch (each CTA its "
+                         "rows and columns), the states in L2; no flush",
                    "graph_steps": chunk},
         "roofline": {"bound": "hbm", "achieved": pt["gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": pt["frac_hbm"], "traffic": None, "peak_source": pk["source"],

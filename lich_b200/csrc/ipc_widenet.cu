@@ -63,7 +63,12 @@ struct WideParams {
   float* energy;
   unsigned* sync;  // [0] arrivals over the launch, [2] abort
   long long* phase_ns;  // [IPC_NET_TRACE_STEPS][IPC_NET_TRACE_PHASES] or null
+  // resident weights (RES): this CTA's P unit's rows of W[l] ([32][res_kp + 8]) and its I unit's
+  // columns of W[l-1] ([res_ki][WN_WI_LD]) stay in shared memory for the whole launch
+  int res_kp, res_ki;
 };
+
+constexpr int WN_WI_LD = 40;  // row stride (elements) of the resident W[l-1] columns: 80 B, ldmatrix conflict-free
 
 // Trace slots of the wide kernel (CTA 0 after the barrier closing each phase).
 enum { WT_START = 0, WT_BATCH = 1, WT_FORWARD = 2, WT_P0 = 3, WT_I0 = 4, WT_ITER = 5, WT_W = 6 };
@@ -212,10 +217,90 @@ __device__ __forceinline__ void wn_ldmatrix_x4_trans(uint32_t (&r)[4], const voi
                : "r"(a));
 }
 
+__device__ __forceinline__ void wn_ldmatrix_x4(uint32_t (&r)[4], const void* p) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+
+// Unit u of a phase over layers [l0, l1] (units of 32 rows, layer by layer): its layer and first row.
+template <typename T>
+__device__ __forceinline__ bool wn_unit(const WideParams<T>& p, int l0, int l1, int u, int& l, int& row0) {
+  if (u < 0) return false;
+  for (l = l0; l <= l1; ++l) {
+    const int n = (p.dims[l] + WN_ROWS - 1) / WN_ROWS;
+    if (u < n) {
+      row0 = u * WN_ROWS;
+      return true;
+    }
+    u -= n;
+  }
+  return false;
+}
+
+// One 16-bit element through L2 (weights change between phases; L1 is not coherent across SMs).
+template <typename T>
+__device__ __forceinline__ T wn_ldcg_t(const T* ptr) {
+  const unsigned short u = __ldcg(reinterpret_cast<const unsigned short*>(ptr));
+  T v;
+  *reinterpret_cast<unsigned short*>(&v) = u;
+  return v;
+}
+
+// Resident rows: Wp[r][k] = W[l][row0 + r][k] of this CTA's P unit (zero outside), row stride res_kp + 8.
+template <typename T>
+__device__ void wn_load_rows(const WideParams<T>& p, T* Wp) {
+  const int ld = p.res_kp + 8, nv = p.res_kp / 8;
+  int l = 0, row0 = 0;
+  const bool has = wn_unit(p, 0, p.L - 1, (int)blockIdx.x, l, row0);
+  const int M = has ? p.dims[l] : 0, K = has ? p.dims[l + 1] : 0;
+  const T* W = has ? p.w[l] : nullptr;
+  for (int i = threadIdx.x; i < WN_ROWS * nv; i += WN_THREADS) {
+    const int r = i / nv, k = (i - r * nv) * 8, m = row0 + r;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (m < M && k < K) {
+      if ((K & 7) == 0) {
+        v = __ldcg(reinterpret_cast<const uint4*>(W + (long long)m * K + k));
+      } else {
+        T* h = reinterpret_cast<T*>(&v);
+        for (int j = 0; j < 8 && k + j < K; ++j) h[j] = wn_ldcg_t(W + (long long)m * K + k + j);
+      }
+    }
+    *reinterpret_cast<uint4*>(Wp + r * ld + k) = v;
+  }
+}
+
+// Resident columns: Wi[k][j] = W[l-1][k][row0 + j] of this CTA's I unit (zero outside), row stride
+// WN_WI_LD; rows [0, res_ki).
+template <typename T>
+__device__ void wn_load_cols(const WideParams<T>& p, T* Wi) {
+  int l = 0, row0 = 0;
+  const bool has = p.L > 1 && wn_unit(p, 1, p.L - 1, (int)blockIdx.x, l, row0);
+  const int M = has ? p.dims[l] : 0, K = has ? p.dims[l - 1] : 0;
+  const T* W = has ? p.w[l - 1] : nullptr;
+  for (int i = threadIdx.x; i < p.res_ki * 4; i += WN_THREADS) {
+    const int k = i >> 2, j = (i & 3) * 8, m = row0 + j;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (k < K && m < M) {
+      if ((M & 7) == 0) {
+        v = __ldcg(reinterpret_cast<const uint4*>(W + (long long)k * M + m));
+      } else {
+        T* h = reinterpret_cast<T*>(&v);
+        for (int q = 0; q < 8 && m + q < M; ++q) h[q] = wn_ldcg_t(W + (long long)k * M + m + q);
+      }
+    }
+    *reinterpret_cast<uint4*>(Wi + k * WN_WI_LD + j) = v;
+  }
+}
+
 // One GEMM phase over layers [l0, l1].  energy != nullptr: add sum_l mean(e[l]^2) (P only).
 // PAIRS (I only, every hidden width even): W_low fragments from 32-bit loads of row pairs.
-template <typename T, int ACT, int MODE, bool PAIRS, bool ACC>
-__device__ void wn_gemm_phase(const WideParams<T>& p, int l0, int l1, float* energy, float* red, T* sT) {
+// RES: this CTA's unit is fixed (P and forward: its P-order unit, I: its I-order unit) and the A
+// fragments come from the resident copies (Wp rows for P / forward, Wi columns for I) by ldmatrix.
+template <typename T, int ACT, int MODE, bool PAIRS, bool ACC, bool RES = false>
+__device__ void wn_gemm_phase(const WideParams<T>& p, int l0, int l1, float* energy, float* red, T* sT,
+                              const T* Wp = nullptr, const T* Wi = nullptr) {
   constexpr int KSTEPS = 8;  // k16 steps whose W fragments a warp loads before using any
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gq = lane >> 2, tq = lane & 3;
@@ -225,7 +310,12 @@ __device__ void wn_gemm_phase(const WideParams<T>& p, int l0, int l1, float* ene
   const int lm_k = (lane & 7) + ((lane >> 3) & 1) * 8, lm_n = (lane >> 4) * 8;
   int total = 0;
   for (int l = l0; l <= l1; ++l) total += (p.dims[l] + WN_ROWS - 1) / WN_ROWS;
-  for (int u = blockIdx.x; u < total; u += gridDim.x) {
+  // forward phases (one layer) on resident rows: the unit is this CTA's P-order unit, if in layer l0
+  int ubase = 0;
+  if (RES && MODE == WN_F)
+    for (int l = 0; l < l0; ++l) ubase += (p.dims[l] + WN_ROWS - 1) / WN_ROWS;
+  for (int u = (int)blockIdx.x - ubase; u < total; u += gridDim.x) {
+    if (u < 0) continue;
     int l = l0, r = u;
     while (r >= (p.dims[l] + WN_ROWS - 1) / WN_ROWS) {
       r -= (p.dims[l] + WN_ROWS - 1) / WN_ROWS;
@@ -262,7 +352,9 @@ __device__ void wn_gemm_phase(const WideParams<T>& p, int l0, int l1, float* ene
     // the first block of W fragments is in flight while the thin operand is staged
     for (int kb = kb0; kb < kb1 || !staged; kb += 16 * KSTEPS) {
       uint32_t a[KSTEPS][4];
-      if constexpr (pairs) {
+      if constexpr (RES) {
+        // A fragments come from shared memory right before their MMA (below)
+      } else if constexpr (pairs) {
         const int mp = row0 + 16 * tile + 2 * gq;
 #pragma unroll
         for (int st = 0; st < KSTEPS; ++st) {
@@ -299,6 +391,13 @@ __device__ void wn_gemm_phase(const WideParams<T>& p, int l0, int l1, float* ene
 #pragma unroll
       for (int st = 0; st < KSTEPS; ++st) {
         if (kb + 16 * st >= kb1) break;
+        if constexpr (RES) {
+          const int k16 = kb + 16 * st, mat = lane >> 3, rr = lane & 7;
+          if constexpr (MODE == WN_I)  // A(m, k) = Wi[k][m]: transposed 8x8 blocks
+            wn_ldmatrix_x4_trans(a[st], Wi + (k16 + rr + (mat >> 1) * 8) * WN_WI_LD + 16 * tile + (mat & 1) * 8);
+          else  // A(m, k) = Wp[m][k]
+            wn_ldmatrix_x4(a[st], Wp + (16 * tile + rr + (mat & 1) * 8) * (p.res_kp + 8) + k16 + (mat >> 1) * 8);
+        }
         uint32_t b[4];  // b0, b1 of n-tile 0, then of n-tile 1
         const int k = kb + 16 * st + lm_k;
         wn_ldmatrix_x4_trans(b, sT + wn_swz(k, lm_n));
@@ -349,8 +448,10 @@ __device__ void wn_gemm_phase(const WideParams<T>& p, int l0, int l1, float* ene
 // W[l] = cast(W[l] + alpha e[l] f(x[l+1])^T) for every layer.  dW of a 16 x 8 tile is one
 // mma.sync m16n8k16 with the batch (B <= 16, zero-padded) as the reduction: A = the unit's rows of
 // e[l] (sE[32][16]), B(n, c) = f(x[l+1])[c][n] straight from the staged rows of sT.
-template <typename T, int ACT, bool ACC>
-__device__ void wn_weight_phase(const WideParams<T>& p, T* sE, T* sT) {
+// RES: the unit is this CTA's P-order unit and W is read from (and written back to) its resident
+// rows as well as global memory.
+template <typename T, int ACT, bool ACC, bool RES = false>
+__device__ void wn_weight_phase(const WideParams<T>& p, T* sE, T* sT, T* Wp = nullptr) {
   constexpr int NT = 8;  // n-tiles whose W values a warp loads before updating any
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gq = lane >> 2, tq = lane & 3;
@@ -393,8 +494,14 @@ __device__ void wn_weight_phase(const WideParams<T>& p, T* sE, T* sT) {
         const int c = (j0 + q * WN_KSLICES) * 8 + 2 * tq;
         w0[q] = w1[q] = 0u;
         if (even && c < K) {
-          if (m0 < M) w0[q] = __ldcg(reinterpret_cast<const uint32_t*>(W + m0 * K + c));
-          if (m1 < M) w1[q] = __ldcg(reinterpret_cast<const uint32_t*>(W + m1 * K + c));
+          if constexpr (RES) {
+            const int ld = p.res_kp + 8;
+            if (m0 < M) w0[q] = *reinterpret_cast<const uint32_t*>(Wp + (mt * 16 + gq) * ld + c);
+            if (m1 < M) w1[q] = *reinterpret_cast<const uint32_t*>(Wp + (mt * 16 + gq + 8) * ld + c);
+          } else {
+            if (m0 < M) w0[q] = __ldcg(reinterpret_cast<const uint32_t*>(W + m0 * K + c));
+            if (m1 < M) w1[q] = __ldcg(reinterpret_cast<const uint32_t*>(W + m1 * K + c));
+          }
         }
       }
 #pragma unroll
@@ -412,12 +519,14 @@ __device__ void wn_weight_phase(const WideParams<T>& p, T* sE, T* sT) {
             h[0] = St<T>::st(St<T>::ld(h[0]) + p.alpha * d[0]);
             h[1] = St<T>::st(St<T>::ld(h[1]) + p.alpha * d[1]);
             *reinterpret_cast<uint32_t*>(W + m0 * K + c) = w0[q];
+            if constexpr (RES) *reinterpret_cast<uint32_t*>(Wp + (mt * 16 + gq) * (p.res_kp + 8) + c) = w0[q];
           }
           if (c < K && m1 < M) {
             T* h = reinterpret_cast<T*>(&w1[q]);
             h[0] = St<T>::st(St<T>::ld(h[0]) + p.alpha * d[2]);
             h[1] = St<T>::st(St<T>::ld(h[1]) + p.alpha * d[3]);
             *reinterpret_cast<uint32_t*>(W + m1 * K + c) = w1[q];
+            if constexpr (RES) *reinterpret_cast<uint32_t*>(Wp + (mt * 16 + gq + 8) * (p.res_kp + 8) + c) = w1[q];
           }
         } else {
 #pragma unroll
@@ -425,6 +534,11 @@ __device__ void wn_weight_phase(const WideParams<T>& p, T* sE, T* sT) {
             if (c + h >= K) continue;
             if (m0 < M) W[m0 * K + c + h] = St<T>::st(ldcg(W + m0 * K + c + h) + p.alpha * d[h]);
             if (m1 < M) W[m1 * K + c + h] = St<T>::st(ldcg(W + m1 * K + c + h) + p.alpha * d[2 + h]);
+            if constexpr (RES) {
+              const int ld = p.res_kp + 8;
+              if (m0 < M) Wp[(mt * 16 + gq) * ld + c + h] = W[m0 * K + c + h];
+              if (m1 < M) Wp[(mt * 16 + gq + 8) * ld + c + h] = W[m1 * K + c + h];
+            }
           }
         }
       }
@@ -433,16 +547,22 @@ __device__ void wn_weight_phase(const WideParams<T>& p, T* sE, T* sT) {
   }
 }
 
-template <typename T, int ACT, bool PAIRS, bool ACC>
+template <typename T, int ACT, bool PAIRS, bool ACC, bool RES>
 __global__ void __launch_bounds__(WN_THREADS, 1) wide_net_kernel(const __grid_constant__ WideParams<T> p) {
   extern __shared__ __align__(16) uint8_t wn_smem[];
   float* red = reinterpret_cast<float*>(wn_smem);                 // [16 warps][16][16] fp32
   T* sE = reinterpret_cast<T*>(red + WN_WARPS * 16 * WN_NC);      // [32][16]
   T* sT = sE + WN_ROWS * WN_NC;                                   // [kmax][16], swizzled halves
+  T* Wp = sT + p.kmax * WN_NC;                                    // RES: [32][res_kp + 8]
+  T* Wi = Wp + WN_ROWS * (p.res_kp + 8);                          // RES: [res_ki][WN_WI_LD]
   const int L = p.L, B = p.B;
   unsigned epoch = 0;  // grid barriers passed in this launch
   if (B < WN_NC)  // batch columns past B stay zero for the whole launch (staging never writes them)
     for (int i = threadIdx.x; i < p.kmax * WN_NC; i += WN_THREADS) sT[i] = St<T>::st(0.f);
+  if constexpr (RES) {  // this CTA's rows of its P unit and columns of its I unit, for the whole launch
+    wn_load_rows(p, Wp);
+    wn_load_cols(p, Wi);
+  }
   __syncthreads();
   for (int step = 0; step < p.steps; ++step) {
     long long* tr = (p.phase_ns != nullptr && step < IPC_NET_TRACE_STEPS && blockIdx.x == 0 && threadIdx.x == 0)
@@ -477,26 +597,30 @@ __global__ void __launch_bounds__(WN_THREADS, 1) wide_net_kernel(const __grid_co
     if (tr) tr[WT_BATCH] = wn_now();
     if (p.forward_init) {
       for (int l = L - 1; l >= 1; --l) {
-        wn_gemm_phase<T, ACT, WN_F, false, ACC>(p, l, l, nullptr, red, sT);
+        wn_gemm_phase<T, ACT, WN_F, false, ACC, RES>(p, l, l, nullptr, red, sT, Wp, Wi);
         if (!wn_grid_sync(p.sync, epoch)) return;
       }
     }
     if (tr) tr[WT_FORWARD] = wn_now();
     for (int t = 0; t < p.T_it; ++t) {
       float* en = (t == p.T_it - 1 && p.energy != nullptr) ? p.energy + step : nullptr;
-      wn_gemm_phase<T, ACT, WN_P, false, ACC>(p, 0, L - 1, en, red, sT);
+      wn_gemm_phase<T, ACT, WN_P, false, ACC, RES>(p, 0, L - 1, en, red, sT, Wp, Wi);
       if (!wn_grid_sync(p.sync, epoch)) return;
       if (tr && t == 0) tr[WT_P0] = wn_now();
       if (L > 1) {
-        wn_gemm_phase<T, ACT, WN_I, PAIRS, ACC>(p, 1, L - 1, nullptr, red, sT);
+        wn_gemm_phase<T, ACT, WN_I, PAIRS, ACC, RES>(p, 1, L - 1, nullptr, red, sT, Wp, Wi);
         if (!wn_grid_sync(p.sync, epoch)) return;
       }
       if (tr && t == 0) tr[WT_I0] = wn_now();
     }
     if (tr) tr[WT_ITER] = wn_now();
     if (p.update_weights) {
-      wn_weight_phase<T, ACT, ACC>(p, sE, sT);
+      wn_weight_phase<T, ACT, ACC, RES>(p, sE, sT, Wp);
       if (!wn_grid_sync(p.sync, epoch)) return;
+      if constexpr (RES) {  // the resident columns were updated by their rows' CTAs: reload them
+        wn_load_cols(p, Wi);
+        __syncthreads();
+      }
     }
     if (tr) tr[WT_W] = wn_now();
   }
@@ -550,10 +674,10 @@ int wn_prepare(WideParams<T>& p, const ipc_net_t* net, const ipc_net_run_t* run,
   return IPC_OK;
 }
 
-template <typename T, int ACT, bool PAIRS, bool ACC>
+template <typename T, int ACT, bool PAIRS, bool ACC, bool RES = false>
 int wn_launch(const WideParams<T>& p, size_t smem, cudaStream_t s) {
-  auto kern = wide_net_kernel<T, ACT, PAIRS, ACC>;
-  cudaError_t err = ensure_kernel_smem<wide_net_kernel<T, ACT, PAIRS, ACC>>((int)smem);
+  auto kern = wide_net_kernel<T, ACT, PAIRS, ACC, RES>;
+  cudaError_t err = ensure_kernel_smem<wide_net_kernel<T, ACT, PAIRS, ACC, RES>>((int)smem);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "wide net kernel smem attribute: %s", cudaGetErrorString(err));
   int dev = 0, sms = 0, per_sm = 0;
   cudaGetDevice(&dev);
@@ -616,7 +740,35 @@ int wide_net_train(const ipc_net_t* net, const ipc_net_run_t* run, cudaStream_t 
     wn_prepare(p, net, run, &smem);
     bool pairs = true;  // every state-update width even: row-pair loads of W_low
     for (int l = 1; l < net->L; ++l) pairs = pairs && (net->dims[l] % 2 == 0);
+    // resident weights: with at most one P unit and one I unit per CTA (one CTA per SM), each CTA keeps
+    // its P unit's rows of W[l] and its I unit's columns of W[l-1] in shared memory for the launch, so
+    // no phase reads W from L2 (the weight phase updates the rows in place and the columns are
+    // reloaded once per step)
+    int sms = 0;
+    {
+      int dev = 0;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    int total_p = 0, total_i = 0, kp = 16, ki = 16;
+    for (int l = 0; l < net->L; ++l) {
+      total_p += (net->dims[l] + WN_ROWS - 1) / WN_ROWS;
+      kp = max(kp, net->dims[l + 1]);
+      if (l >= 1) {
+        total_i += (net->dims[l] + WN_ROWS - 1) / WN_ROWS;
+        ki = max(ki, net->dims[l - 1]);
+      }
+    }
+    kp = (kp + 15) & ~15;
+    ki = (ki + 15) & ~15;
+    const size_t smem_res = smem + (size_t)WN_ROWS * (kp + 8) * sizeof(TT) + (size_t)ki * WN_WI_LD * sizeof(TT);
+    const bool res = p.acache && total_p <= sms && total_i <= sms && smem_res + 256 <= 227u * 1024u;
     IPC_DISPATCH_ACT(run->act, AC, {
+      if (res) {
+        p.res_kp = kp;
+        p.res_ki = ki;
+        return wn_launch<TT, AC, false, true, true>(p, smem_res, s);
+      }
       if (p.acache)
         return pairs ? wn_launch<TT, AC, true, true>(p, smem, s) : wn_launch<TT, AC, false, true>(p, smem, s);
       return pairs ? wn_launch<TT, AC, true, false>(p, smem, s) : wn_launch<TT, AC, false, false>(p, smem, s);

@@ -9,7 +9,8 @@
 * dW of the weight phase from random hidden states (O(1) errors) against the fp32 oracle, 2e-2.
 * Several steps over a device pool, per-step energy against the oracle's energy metric.
 * Shapes the cluster kernel does not take: B = 4 at hidden 64, odd widths (tails in every
-  dimension), a one-layer network.
+  dimension), a one-layer network; with the weights resident in shared memory (each CTA's rows and
+  columns, every shape above) and without (4096-wide rows; more units than CTAs).
 * Failure detection: the barrier-timeout self-test makes one CTA's grid-barrier wait expire
   (a CTA that never arrives), the status reads IPC_ERR_TIMEOUT, and the context keeps working.
 """
@@ -147,7 +148,10 @@ def test_pool_steps_and_energy():
     assert ((got - ref).abs() / ref.abs()).max().item() <= 2e-2
 
 
-@pytest.mark.parametrize("dims,B", [((10, 64, 64, 784), 4), ((7, 100, 33, 250), 5), ((12, 300), 16)])
+# the last two shapes: W rows of 4096 do not fit the resident copies (the kernel reads W from L2),
+# and more 32-row units than CTAs (every CTA takes several units per phase)
+@pytest.mark.parametrize("dims,B", [((10, 64, 64, 784), 4), ((7, 100, 33, 250), 5), ((12, 300), 16),
+                                    ((10, 4096, 784), 4), ((10, 1024, 1024, 2048, 1024, 784), 4)])
 def test_shapes_outside_the_cluster_kernel(dims, B):
     dtype, alpha, T = torch.float16, 0.02, 4
     w0, pool = _inputs(dims, B, seed=70 + B)
