@@ -40,6 +40,7 @@
 // reads the word).
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <cstring>
@@ -1018,11 +1019,12 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   int cap = grid_cap();
   if (tune != nullptr && tune->max_ctas > 0 && tune->max_ctas < cap) cap = tune->max_ctas;
   const int want = tune != nullptr ? tune->splits : 0;  // 0: heuristic, 1: never, >= 2: requested
-  if ((MODE == MODE_W || MODE == MODE_WD || MODE == MODE_WO) && !PAIR && ws != nullptr && want != 1 &&
-      (want >= 2 || (p.tiles < cap / 2 && nk >= 8)) &&
+  const int units = PAIR ? max(1, cap / 2) : cap;  // tiles walked at once: CTAs, or CTA pairs
+  if ((MODE == MODE_W || MODE == MODE_WD || MODE == MODE_WO) && ws != nullptr && want != 1 &&
+      (want >= 2 || (p.tiles < units / 2 && nk >= 8)) &&
       a.gsOut == (long long)a.Mg * a.Ng) {  // the reduce pass walks out as one dense [groups][M][N] array
     const long long tile_bytes = (long long)a.groups * a.Mg * a.Ng * 4;
-    int splits = want >= 2 ? min(want, nk) : min(cap / p.tiles, nk / 4);  // heuristic: one wave of units
+    int splits = want >= 2 ? min(want, nk) : min(units / p.tiles, nk / 4);  // heuristic: one wave of units
     const long long fit = (long long)(ws_bytes / (size_t)tile_bytes);
     if (fit < splits) splits = (int)fit;
     if (splits >= 2) {
@@ -1036,7 +1038,8 @@ int launch_tc_t(const GemmArgs& a, int dtype, cudaStream_t s, float* ws, size_t 
   // 3.5 with halves); taken for a saving of >= 5 % of the tile time (or on request, tc_splits >= 2)
   p.atomic = 0;
   p.mcast = a.mcast;
-  if (MODE == MODE_WD && PAIR && !a.accumulate && want != 1 && nk >= 16 && a.gsOut == (long long)a.Mg * a.Ng) {
+  if (MODE == MODE_WD && PAIR && p.splits == 1 && !a.accumulate && want != 1 && nk >= 16 &&
+      a.gsOut == (long long)a.Mg * a.Ng) {
     const long long units = cap / 2 > 0 ? cap / 2 : 1;
     const long long w1 = (p.tiles + units - 1) / units, w2 = (2LL * p.tiles + units - 1) / units;
     if (want >= 2 || w2 * 20 <= 2 * w1 * 19) {
@@ -1190,12 +1193,27 @@ int launch_tc(const GemmArgs& a, int mode, int act, int dtype, cudaStream_t s, f
   // the rows (measured at 4096^2 x 8192: P 0.81 -> 0.89 of the cuBLAS burst, I 0.69 -> 0.81, W 0.75 ->
   // 0.84; each SM reads half the B operand from shared memory), over cap/2 pairs; so the estimate is
   // ceil(pair tiles / (cap / 2)) x 0.9 x (256 + 416).  Rows beyond M in a pair's second half are padding
-  // (M = 384: single CTAs win).  Weight updates that split the batch stay on single CTAs.
+  // (M = 384: single CTAs win).
   const long long tp = ((a.Mg + 255) / 256) * ((a.Ng + 255) / 256) * a.groups;
   const long long cost_pair = ((tp + cap / 2 - 1) / (cap / 2)) * (256 + 416) * 9 / 10;
   bool pair = a.Ng >= 256 && !splitk && cap >= 2 && cost_pair < (cost256 < cost128 ? cost256 : cost128);
+  // a split weight update on pairs: s batch ranges per pair tile over cap/2 pairs against per 128 x 256
+  // tile over cap CTAs (each range 1/s of a tile time; workspace bounds s): 1024^2 x 65536 splits 16 pair
+  // tiles 4 ways on 74 pairs instead of 32 tiles 4 ways on 148 CTAs, at 0.9 of the tile time
+  if (splitk && a.Ng >= 256 && cap >= 4) {
+    const long long nk = (a.Kg + TC_BK - 1) / TC_BK;
+    const long long fit = (long long)(ws_bytes / (size_t)(4LL * a.groups * a.Mg * a.Ng));
+    const long long u2 = cap / 2;
+    const long long s1 = std::min(std::min((long long)cap / t256, nk / 4), fit);
+    const long long s2 = std::min(std::min(u2 / tp, nk / 4), fit);
+    if (s1 >= 2 && s2 >= 2) {
+      const long long c1 = ((t256 * s1 + cap - 1) / cap) * (256 + 416) * 10 / s1;
+      const long long c2 = ((tp * s2 + u2 - 1) / u2) * (256 + 416) * 9 / s2;
+      pair = c2 < c1;
+    }
+  }
   if (tune != nullptr && tune->pair == 1) pair = false;
-  if (tune != nullptr && tune->pair == 2) pair = a.Ng >= 256 && !splitk;
+  if (tune != nullptr && tune->pair == 2) pair = a.Ng >= 256;
   if (tune != nullptr && tune->bn == 128) pair = false;
   if (pair)
     return dtype == IPC_DT_F16 ? dispatch_mode<__half, 256, 1>(a, mode, act, dtype, s, ws, ws_bytes, tune)
