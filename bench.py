@@ -418,6 +418,14 @@ def run_c2_e2e(args, model, dims, B, T, dtype, dev, rank, world):
     comp = torch.cuda.current_stream(dev)
     w_init = [w.clone() for w in model.w]
     source = ((x_h, y_h) for _ in range(steps // chunk))  # pool chunks of 64 pinned batches (Ph == chunk)
+    # one untimed pass of the loop body (the pipeline's device slots and streams, the energy read-back)
+    warm = BatchPipeline(((x_h, y_h) for _ in range(2)), device=dev, dtype=dtype, num_classes=dims[0], depth=2,
+                         steps_per_slot=chunk)
+    for c, (px, py) in enumerate(warm):
+        model.train_pool(px, py, steps=int(px.shape[0]), T=T, energy=energy[c % 2])
+        energy_h[:int(px.shape[0])].copy_(energy[c % 2][:int(px.shape[0])], non_blocking=True)
+    for w, w0 in zip(model.w, w_init):
+        w.copy_(w0)
     torch.cuda.synchronize(dev)
     barrier(world)
     start = torch.cuda.Event(enable_timing=True)

@@ -77,6 +77,7 @@ struct NetParams {
   int pool_batches, first_batch, steps, T_it, forward_init, update_weights;
   float alpha, gamma;
   float* energy;
+  float inv_cnt[MAXL + 1];  // 1 / (dims[l] * B): layer l's weight in the energy sum_l mean(e[l]^2)
   long long* phase_ns;
   // shared-memory layout, byte offsets
   int o_w[MAXL], o_x[MAXL], o_a[MAXL], o_e[MAXL];
@@ -395,7 +396,7 @@ __device__ __forceinline__ void async_state(uint8_t* smem, int off, const T* g, 
   }
 }
 
-template <typename T, int ACT, int NCOL>
+template <typename T, int ACT, int NCOL, bool EN>
 __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_constant__ NetParams<T> p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int NT = NCOL / 8;   // n8 tiles per CTA column block
@@ -598,7 +599,11 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
     trace(step, 4);
 
     // ---- T inference iterations ----
+    // the energy of the last iteration accumulates in the P phase where each e is produced (a second pass
+    // over the e tiles after the iterations cost ~2.8 us of a 25 us step at configs[1])
+    float esq = 0.f;
     for (int t = 0; t < p.T_it; ++t) {
+      const bool want_e = EN && t == p.T_it - 1;  // EN: a launch that reports energy
       // P: e[l] = cast(x[l]) - cast(W[l] f(x[l+1])), l < L-1 on tensor cores; the input layer uses mu
       {
         int base = 0;
@@ -630,7 +635,12 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
               const int rr = mt * 16 + gq + 8 * h;
               if (rr >= p.dims[l]) continue;
               const int i = sw<NCOL>(rr, c);
-              U32(p.o_e[l], i) = Pk<T>::sub(U32(p.o_x[l], i), Pk<T>::pack(acc[2 * h], acc[2 * h + 1]));
+              const uint32_t ev = Pk<T>::sub(U32(p.o_x[l], i), Pk<T>::pack(acc[2 * h], acc[2 * h + 1]));
+              U32(p.o_e[l], i) = ev;
+              if (want_e) {
+                const float2 f = Pk<T>::unpack(ev);
+                esq = fmaf(fmaf(f.x, f.x, f.y * f.y), p.inv_cnt[l], esq);
+              }
             }
           }
           base += units;
@@ -638,7 +648,12 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
         for (int it = threadIdx.x; it < dT * (NCOL / 2); it += NET_THREADS) {
           const int r = it / (NCOL / 2), c = (it % (NCOL / 2)) * 2;
           const int i = sw<NCOL>(r, c);
-          U32(p.o_e[Lt], i) = Pk<T>::sub(U32(p.o_x[Lt], i), U32(p.o_mu, i));
+          const uint32_t ev = Pk<T>::sub(U32(p.o_x[Lt], i), U32(p.o_mu, i));
+          U32(p.o_e[Lt], i) = ev;
+          if (want_e) {
+            const float2 f = Pk<T>::unpack(ev);
+            esq = fmaf(fmaf(f.x, f.x, f.y * f.y), p.inv_cnt[Lt], esq);
+          }
         }
       }
       __syncthreads();
@@ -686,16 +701,8 @@ __global__ void __launch_bounds__(NET_THREADS, 1) net_kernel_act(const __grid_co
     trace(step, 5);
 
     // ---- energy of the last iteration: sum_l mean(e[l]^2) (reference.py:58) ----
-    if (p.energy != nullptr) {
-      float part = 0.f;
-      for (int l = 0; l <= Lt; ++l) {
-        float sl = 0.f;
-        for (int it = threadIdx.x; it < p.dims[l] * NCOL; it += NET_THREADS) {
-          const float v = St<T>::ld(S(p.o_e[l])[sw<NCOL>(it / NCOL, it % NCOL)]);
-          sl = fmaf(v, v, sl);
-        }
-        part += sl / ((float)p.dims[l] * (float)B);
-      }
+    if constexpr (EN) {
+      float part = esq;  // this thread's e^2 of the last iteration, each weighted 1 / (dims[l] * B)
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
       if (lane == 0) atomicAdd(p.energy + (long long)step * p.nets + net, part);
@@ -965,10 +972,10 @@ int choose_plan(NetParams<T>& p, int want, int* ncol_out) {
                    want > 0 ? " with the requested cluster size" : "");
 }
 
-template <typename T, int ACT, int NCOL>
+template <typename T, int ACT, int NCOL, bool EN>
 int launch_net_t(NetParams<T>& p, cudaStream_t s) {
-  auto kern = net_kernel_act<T, ACT, NCOL>;
-  cudaError_t err = ensure_kernel_smem<net_kernel_act<T, ACT, NCOL>>(p.smem_bytes, p.C > MAX_PORTABLE_CLUSTER);
+  auto kern = net_kernel_act<T, ACT, NCOL, EN>;
+  cudaError_t err = ensure_kernel_smem<net_kernel_act<T, ACT, NCOL, EN>>(p.smem_bytes, p.C > MAX_PORTABLE_CLUSTER);
   if (err != cudaSuccess) return set_error(IPC_ERR_CUDA, "net kernel smem attribute: %s", cudaGetErrorString(err));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.C, p.nets, 1);
@@ -1018,15 +1025,16 @@ int run_net(const ipc_net_t* net, const ipc_net_run_t* run, cudaStream_t s) {
   p.alpha = run->alpha;
   p.gamma = run->gamma;
   p.energy = run->energy;
+  for (int l = 0; l <= p.L; ++l) p.inv_cnt[l] = 1.f / ((float)p.dims[l] * (float)p.B);
   p.phase_ns = run->phase_ns;
   int ncol = 0;
   int rc = choose_plan(p, run->cluster, &ncol);
   if (rc) return rc;
   IPC_DISPATCH_ACT(run->act, AC, {
     switch (ncol) {
-      case 8: rc = launch_net_t<T, AC, 8>(p, s); break;
-      case 16: rc = launch_net_t<T, AC, 16>(p, s); break;
-      default: rc = launch_net_t<T, AC, 32>(p, s); break;
+      case 8: rc = p.energy ? launch_net_t<T, AC, 8, true>(p, s) : launch_net_t<T, AC, 8, false>(p, s); break;
+      case 16: rc = p.energy ? launch_net_t<T, AC, 16, true>(p, s) : launch_net_t<T, AC, 16, false>(p, s); break;
+      default: rc = p.energy ? launch_net_t<T, AC, 32, true>(p, s) : launch_net_t<T, AC, 32, false>(p, s); break;
     }
   });
   return rc;
