@@ -915,11 +915,13 @@ def run_c4a(args, world, rank, local):
     torch.cuda.synchronize(dev)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
+    h0 = time.perf_counter()
     for i in range(n_e2e):
         xd.copy_(x_h, non_blocking=True)
         yd.copy_(y_h, non_blocking=True)
         model.train_step(xd, yd, T=T)
         m_h[i:i + 1].copy_((model.e[0].float() ** 2).mean().reshape(1), non_blocking=True)
+    host_e2e = (time.perf_counter() - h0) * 1e3
     f1.record(stream)
     torch.cuda.synchronize(dev)
     ms_e2e = max_over_ranks(f0.elapsed_time(f1), world, dev)
@@ -941,6 +943,7 @@ def run_c4a(args, world, rank, local):
         "points": points,
         "e2e": {"value": round(world * n_e2e * B / (ms_e2e * 1e-3), 1), "unit": "samples/s",
                 "h2d_bytes_per_step": int(x_h.numel() + y_h.numel()) * 2, "d2h_bytes_per_step": 4, "steps": n_e2e,
+                "host_issue_ms_per_step": round(host_e2e / n_e2e, 4),
                 "path": "TileLangIPC.train_step (eager launches) on a batch copied from pinned host memory"},
         "gpu_launches": int(r["gpu_launches"]), "clocks": clk.summary(),
     }
